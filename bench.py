@@ -1,0 +1,441 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 ChunkGatedDeltaRuleFwdH (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...        (N > 1)
+
+Workload (default): the north-star configuration -- bf16, B=4, T=8192,
+H=32, K=V=128, chunk 64, h0 ~ 0.1 randn (fp32), final_state stored -- per
+rank, inputs generated on the device from seed + rank (weak scaling: the
+(sequence, head) pairs are independent, so every rank runs its own shard and
+there is no collective on the data path).  ``--config c5`` runs the
+BASELINE's multi-GPU config instead (B=8, T=8192, H=64, K=128, V=256) with
+its (b, h) pairs split evenly over the ranks (strong scaling).
+
+Metric: fwd_h tokens/s (tokens = B*T per call), whole job.  ``value`` is
+device time (CUDA events on the launching stream, max over ranks) with
+inputs resident in HBM; inputs and outputs total ~1.9 GB per rank, far
+beyond the 126 MB L2, so no flush is needed between steps.  ``e2e`` is the
+same metric through the public Python API with pinned host buffers, the
+host->device copy of every input and the device->host copy of every output
+inside the timed region.  ``roofline`` relates the op's algorithmic HBM
+bytes per launch to the measured HBM copy bandwidth.  ``cpu_baseline`` is
+the reference's arithmetic (the CPU oracle, a restatement of the reference
+PyTorch code) timed on this host's cores on a bounded sample.
+
+``--impl reference`` times that CPU implementation alone (rank 0; other
+ranks exit), as the reference arm.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+CONFIGS = {
+    "ns": dict(B=4, T=8192, H=32, HK=32, K=128, V=128, scaling="weak"),
+    "c5": dict(B=8, T=8192, H=64, HK=64, K=128, V=256, scaling="strong"),
+    "c2": dict(B=2, T=4096, H=16, HK=16, K=128, V=128, scaling="weak"),
+    "c3": dict(B=1, T=65536, H=32, HK=32, K=128, V=128, scaling="weak", h0=False),
+}
+
+
+def algorithmic_bytes(B, T, H, HK, K, V, has_h0=True, store_final=True, save_v=True, final_bytes=4, h0_bytes=4):
+    """Each tensor read or written once: k, w, u, g, v_new, h, h0, final."""
+    NT = (T + 63) // 64
+    N = B
+    b = B * T * HK * K * 2 + B * T * H * K * 2 + B * T * H * V * 2 + B * T * H * 4
+    if save_v:
+        b += B * T * H * V * 2
+    b += B * NT * H * K * V * 2
+    if has_h0:
+        b += N * H * K * V * h0_bytes
+    if store_final:
+        b += N * H * K * V * final_bytes
+    return b
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def load_traffic(config):
+    """dram bytes per launch from the committed ncu summary, if any."""
+    p = ROOT / "profiles" / f"traffic_{config}.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text())
+        except Exception:
+            return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle sampling during the timed region."""
+
+    QUERY = ("index,uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuid: str | None):
+        self.uuid = uuid
+        self.proc = None
+        self.t_start = self.t_stop = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(prefix="clocks_", suffix=".csv")
+            os.close(fd)
+            cmd = ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits", "-lms", "50"]
+            if self.uuid:
+                cmd.insert(1, f"--id={self.uuid}")
+            self.proc = subprocess.Popen(cmd, stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def mark(self, which):
+        setattr(self, which, time.time())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.12)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        for line in Path(self.path).read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 10:
+                continue
+            rows.append(parts)
+        os.unlink(self.path)
+        sm = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        mx = [float(r[3]) for r in rows if r[3].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for r in rows:
+            for name, val in zip(names, r[6:10]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+def dist_setup():
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def shard(cfg, world, rank):
+    """Per-rank problem: weak scaling keeps the config per rank; strong
+    scaling splits the (b, h) pairs by heads."""
+    c = dict(cfg)
+    if cfg["scaling"] == "strong" and world > 1:
+        assert cfg["H"] % world == 0
+        c["H"] = cfg["H"] // world
+        c["HK"] = cfg["HK"] // world
+    return c
+
+
+def gen_inputs(c, seed, device):
+    import torch
+    g = torch.Generator(device=device).manual_seed(seed)
+    B, T, H, HK, K, V = c["B"], c["T"], c["H"], c["HK"], c["K"], c["V"]
+    k = torch.randn(B, T, HK, K, device=device, generator=g)
+    k = (k / k.norm(dim=-1, keepdim=True)).to(torch.bfloat16)
+    beta = torch.sigmoid(torch.randn(B, T, H, device=device, generator=g))
+    w = (beta[..., None] * k.float().repeat_interleave(H // HK, dim=2)).to(torch.bfloat16)
+    u = (0.5 * torch.randn(B, T, H, V, device=device, generator=g)).to(torch.bfloat16)
+    gl = torch.nn.functional.logsigmoid(torch.randn(B, T, H, device=device, generator=g) + 2.0)
+    pad = (-T) % 64
+    gl = torch.nn.functional.pad(gl, (0, 0, 0, pad)).view(B, (T + pad) // 64, 64, H).cumsum(2).view(B, T + pad, H)
+    gl = gl[:, :T].contiguous()
+    h0 = (0.1 * torch.randn(B, H, K, V, device=device, generator=g)) if c.get("h0", True) else None
+    return dict(k=k, w=w, u=u, g=gl, initial_state=h0)
+
+
+def cpu_reference_rate(c, budget_s, n_threads, max_pairs=None):
+    """Time the CPU oracle (reference arithmetic) on a bounded sample of the
+    workload: P (sequence, head) pairs x C chunks.  Returns (tokens/s for the
+    whole job, description, threads)."""
+    import numpy as np
+    import torch
+    sys.path.insert(0, str(ROOT / "tests"))
+    from oracle import oracle as o  # the reference arithmetic, restated (timed baseline)
+
+    threads = n_threads or o.max_threads()
+    P = max(1, min(threads, max_pairs or threads, c["B"] * c["H"]))
+    NT = (c["T"] + 63) // 64
+    gen = torch.Generator().manual_seed(0)
+
+    def sample(chunks):
+        T = 64 * chunks
+        k = torch.randn(1, T, P, c["K"], generator=gen)
+        k = (k / k.norm(dim=-1, keepdim=True)).to(torch.bfloat16)
+        w = (torch.sigmoid(torch.randn(1, T, P, 1, generator=gen)) * k.float()).to(torch.bfloat16)
+        u = (0.5 * torch.randn(1, T, P, c["V"], generator=gen)).to(torch.bfloat16)
+        g = torch.nn.functional.logsigmoid(torch.randn(1, T, P, generator=gen) + 2.0)
+        g = g.view(1, chunks, 64, P).cumsum(2).view(1, T, P)
+        h0 = 0.1 * torch.randn(1, P, c["K"], c["V"], generator=gen)
+        bits = lambda t: t.contiguous().view(torch.int16).numpy().view(np.uint16)  # noqa: E731
+        return bits(k), bits(w), bits(u), g.numpy(), h0.numpy()
+
+    def timed(chunks):
+        a = sample(chunks)
+        t0 = time.perf_counter()
+        o.fwd_h(*a, mode="reference", n_threads=threads)
+        return time.perf_counter() - t0
+
+    t1 = timed(1)
+    chunks = int(max(1, min(NT, budget_s / max(t1, 1e-4))))
+    dt = timed(chunks)
+    pair_chunks_per_s = P * chunks / dt
+    job_pair_chunks = c["B"] * c["H"] * NT
+    tokens = c["B"] * c["T"]
+    rate = tokens * pair_chunks_per_s / job_pair_chunks
+    desc = (f"{P} (sequence, head) pairs x {chunks} chunks of the workload ({P * chunks} of "
+            f"{job_pair_chunks} pair-chunks, {dt:.2f} s), scaled linearly to the whole job")
+    return rate, desc, threads
+
+
+def run_reference_arm(args, cfg_name, c, world, rank):
+    if rank != 0:
+        return 0
+    K, W = args.steps, args.warmup
+    budget = max(0.05, min(3.0, 150.0 / max(1, K + W)))
+    rates = []
+    desc, threads = "", 0
+    for i in range(W + K):
+        r, desc, threads = cpu_reference_rate(c, budget, 0)
+        if i >= W:
+            rates.append(r)
+    value = statistics.median(rates)
+    line = {
+        "impl": "reference",
+        "metric": "fwd_h tokens/s",
+        "value": value,
+        "unit": "tokens/s",
+        "n_gpus": args.gpus,
+        "steps": K,
+        "warmup": W,
+        "ms_per_step": 1000.0 * c["B"] * c["T"] / value,
+        "higher_is_better": True,
+        "scaling": c["scaling"],
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic",
+        "config": config_block(cfg_name, c, world),
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": desc},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def config_block(name, c, world):
+    return {
+        "workload": f"{name}: chunk_gated_delta_rule_fwd_h bf16 B={c['B']} T={c['T']} H={c['H']} "
+                    f"K={c['K']} V={c['V']} chunk=64, h0 fp32, final_state fp32, v_new stored"
+                    + (" (per rank)" if c["scaling"] == "weak" else f" (heads split over {world} ranks)"),
+        "B": c["B"], "T": c["T"], "H": c["H"], "K": c["K"], "V": c["V"], "chunk": 64,
+        "tokens_per_step_per_rank": c["B"] * c["T"],
+        "l2": "inputs+outputs ~1.9 GB per rank >> 126 MB L2 (no flush needed)",
+        "parallelism": f"head-sharded x{world}, no collective on the data path",
+    }
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="ns")
+    ap.add_argument("--numerics", choices=["fp32_state", "reference"], default="fp32_state")
+    ap.add_argument("--v-tile", type=int, default=0)
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    cfg = CONFIGS[args.config]
+
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        return run_reference_arm(args, args.config, shard(cfg, 1, 0), world, rank)
+
+    import torch
+    import cann_operator_challenge_august_b200 as cg
+
+    world, rank, local = dist_setup()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    c = shard(cfg, world, rank)
+    inp = gen_inputs(c, seed=1000 + rank, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    opts = dict(numerics=args.numerics, v_tile=args.v_tile)
+
+    def step():
+        return cg.chunk_gated_delta_rule_fwd_h(inp["k"], inp["w"], inp["u"], inp["g"], inp["initial_state"],
+                                               **opts)
+
+    for _ in range(args.warmup):
+        out = step()
+    torch.cuda.synchronize()
+    del out
+    uuid = None
+    try:
+        uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:
+        pass
+    clocks = ClockSampler(uuid)
+    clocks.start()
+    time.sleep(0.3)
+    barrier(world)
+    torch.cuda.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * args.steps)]
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_stop = torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for i in range(args.steps):
+        ev[2 * i].record(stream)
+        out = step()
+        ev[2 * i + 1].record(stream)
+    t_stop.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    clk = clocks.stop()
+    elapsed_ms = t_start.elapsed_time(t_stop)
+    per_launch_ms = sum(ev[2 * i].elapsed_time(ev[2 * i + 1]) for i in range(args.steps)) / args.steps
+    elapsed_ms = max_over_ranks(elapsed_ms, world)
+    per_launch_ms = max_over_ranks(per_launch_ms, world)
+    ms_per_step = elapsed_ms / args.steps
+    tokens_per_step = c["B"] * c["T"] * world
+    value = tokens_per_step / (ms_per_step / 1000.0)
+
+    # ---- e2e: public API with pinned host buffers, copies inside the timed region
+    host = {n: (x.cpu().pin_memory() if x is not None else None) for n, x in inp.items()}
+    h2d = sum(x.numel() * x.element_size() for x in host.values() if x is not None)
+    h_out, v_out, f_out = out
+    host_out = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in (h_out, v_out, f_out)]
+    d2h = sum(t.numel() * t.element_size() for t in host_out)
+    del out, h_out, v_out, f_out
+
+    def e2e_step():
+        d = {n: (x.to(dev, non_blocking=True) if x is not None else None) for n, x in host.items()}
+        o = cg.chunk_gated_delta_rule_fwd_h(d["k"], d["w"], d["u"], d["g"], d["initial_state"], **opts)
+        for dst, src in zip(host_out, o):
+            dst.copy_(src, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world) / args.e2e_steps
+    e2e_value = tokens_per_step / (e2e_ms / 1000.0)
+
+    nbytes = algorithmic_bytes(c["B"], c["T"], c["H"], c["HK"], c["K"], c["V"], has_h0=inp["initial_state"] is not None)
+    peak, peak_kind = load_peaks()
+    achieved = nbytes / (per_launch_ms / 1000.0) / 1e9
+    traffic = load_traffic(args.config)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rate, desc, threads = cpu_reference_rate(c, 12.0, 0)
+        cpu = {"value": rate, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": desc}
+
+    if rank == 0:
+        line = {
+            "metric": "fwd_h tokens/s",
+            "value": value,
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms_per_step,
+            "higher_is_better": True,
+            "scaling": c["scaling"],
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded, generated on device per rank)",
+            "numerics": args.numerics,
+            "config": config_block(args.config, c, world),
+            "gpu_launches": args.steps,
+            "roofline": {
+                "bound": "hbm",
+                "achieved": achieved,
+                "peak": peak,
+                "unit": "GB/s",
+                "frac": achieved / peak,
+                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
+                "algorithmic_bytes_per_launch": nbytes,
+                "launch_ms": per_launch_ms,
+                "traffic": traffic.get("dram_bytes_per_launch") if traffic else None,
+            },
+            "hbm_gbs_per_gpu": achieved,
+            "clocks": clk,
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": e2e_ms},
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

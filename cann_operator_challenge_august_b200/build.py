@@ -1,0 +1,65 @@
+"""Build recipe for the in-tree CUDA library (sm_100a only).
+
+    python -m cann_operator_challenge_august_b200.build     # or build() from Python
+
+produces ``cann_operator_challenge_august_b200/libcgdr_fwd_h.so``: the C ABI
+of include/cgdr_fwd_h.h with the tensor-core and general kernels.  nvcc
+cross-compiles without a GPU.
+"""
+
+from __future__ import annotations
+
+import os
+import shutil
+import subprocess
+import sys
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+ROOT = PKG.parent
+LIB = PKG / "libcgdr_fwd_h.so"
+SOURCES = [PKG / "csrc" / "cgdr_fwd_h.cu"]
+HEADERS = sorted((PKG / "csrc").glob("*.cuh")) + [ROOT / "include" / "cgdr_fwd_h.h"]
+
+NVCC_FLAGS = [
+    "-gencode", "arch=compute_100a,code=sm_100a",
+    "-lineinfo", "-O3", "-std=c++17",
+    "-Xcompiler", "-fPIC,-O3",
+    "-Xptxas", "-v",
+    "--expt-relaxed-constexpr",
+    "-shared",
+]
+
+
+def nvcc() -> str:
+    for cand in (os.environ.get("NVCC"), shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"):
+        if cand and Path(cand).exists():
+            return cand
+    raise RuntimeError("nvcc not found: the CUDA library cannot be built")
+
+
+def needs_build() -> bool:
+    if not LIB.exists():
+        return True
+    t = LIB.stat().st_mtime
+    return any(src.stat().st_mtime > t for src in SOURCES + HEADERS)
+
+
+def build(force: bool = False, verbose: bool = False) -> Path:
+    if not force and not needs_build():
+        return LIB
+    cmd = [nvcc(), *NVCC_FLAGS, "-o", str(LIB), *map(str, SOURCES)]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    log = PKG / "build.log"
+    log.write_text(" ".join(cmd) + "\n" + res.stdout + res.stderr)
+    if res.returncode != 0:
+        sys.stderr.write(res.stdout + res.stderr)
+        raise RuntimeError(f"nvcc failed (exit {res.returncode}); see {log}")
+    if verbose:
+        sys.stdout.write(res.stderr)
+    return LIB
+
+
+if __name__ == "__main__":
+    build(force="--force" in sys.argv, verbose=True)
+    print(LIB)

@@ -1,0 +1,150 @@
+// Shared definitions of the ChunkGatedDeltaRuleFwdH kernels: the launch
+// parameter block and the element-wise arithmetic of the two numerics modes.
+#pragma once
+
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+namespace cgdr {
+
+constexpr int kChunk = 64;  // BT, fixed by the op (def.cpp:72-74)
+
+enum IoType : int32_t { kBF16 = 1, kF32 = 2 };
+
+// Everything a kernel needs, by value.  Strides are in elements; the
+// innermost dimension of every tensor is contiguous.  "t" strides address
+// tokens (global, packed for varlen), "h" strides address heads.
+struct FwdHParams {
+    const void* k;
+    const void* w;
+    const void* u;
+    const float* g;
+    const void* h0;
+    const int64_t* cu_seqlens;     // varlen only
+    const int64_t* chunk_offsets;  // caller-supplied (optional, varlen)
+    void* h;
+    void* v_new;                   // nullptr: save_new_value = False
+    void* final_state;             // nullptr: not stored
+    int* status;                   // device status word (workspace)
+    const int32_t* seq_chunk_base; // workspace: chunk offset of each sequence (varlen)
+    const int32_t* seq_order;      // workspace: sequences longest first (varlen)
+
+    int64_t B, T, HK, H, K, V, N, NT;
+    int64_t k_sb, k_st, k_sh;
+    int64_t w_sb, w_st, w_sh;
+    int64_t u_sb, u_st, u_sh;
+    int64_t g_sb, g_st, g_sh;
+    int64_t v_sb, v_st, v_sh;
+    int64_t h_sb, h_sc, h_sh, h_sk;
+    int64_t h0_sn, h0_sh, h0_sk;
+    int64_t f_sn, f_sh, f_sk;
+
+    int32_t io_dtype;     // IoType of k, w, u, h, v_new
+    int32_t h0_dtype;     // IoType of initial_state
+    int32_t f_dtype;      // IoType of final_state
+    int32_t numerics;     // 0 reference, 1 fp32 state
+    int32_t use_g;
+    int32_t varlen;
+    int32_t v_tile;
+    int32_t n_vtiles;
+    int32_t fault_inject;
+    int32_t pad_;
+    uint64_t timeout_ns;
+};
+
+// Sequence geometry of one task.
+struct SeqInfo {
+    int64_t b;      // batch row of k/w/u/g/v/h
+    int64_t bos;    // first token (within the batch row)
+    int64_t len;    // tokens
+    int64_t boh;    // chunk index of the sequence's first chunk in h
+    int64_t n;      // sequence index (initial/final state row)
+};
+
+__device__ __forceinline__ SeqInfo seq_info(const FwdHParams& p, int64_t n)
+{
+    SeqInfo s;
+    s.n = n;
+    if (p.varlen) {
+        s.b = 0;
+        s.bos = p.cu_seqlens[n];
+        s.len = p.cu_seqlens[n + 1] - s.bos;
+        s.boh = p.chunk_offsets ? p.chunk_offsets[n] : p.seq_chunk_base[n];
+    } else {
+        s.b = n;
+        s.bos = 0;
+        s.len = p.T;
+        s.boh = 0;
+    }
+    return s;
+}
+
+// ---- scalar arithmetic of the reference rounding chain --------------------------
+// generate_golden.py:287-292 (cast_to_float16) and :414-441 (chunk update).
+// The __f*_rn intrinsics keep every product and sum separately rounded (the
+// compiler may not contract them into an FMA that the reference never does).
+
+__device__ __forceinline__ float bf16_bits_to_f32(uint32_t b16) { return __uint_as_float(b16 << 16); }
+
+__device__ __forceinline__ float round_bf16(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+__device__ __forceinline__ float round_f16(float x) { return __half2float(__float2half_rn(x)); }
+
+// cast_to_float16: round to fp16; finite values beyond the fp16 range
+// saturate to +-65504 while inf and NaN pass through.
+__device__ __forceinline__ float cast_f16(float x)
+{
+    const float c = fabsf(x) < INFINITY ? fminf(fmaxf(x, -65504.0f), 65504.0f) : x;
+    return round_f16(c);
+}
+
+__device__ __forceinline__ float nan_to_zero(float x) { return x != x ? 0.0f : x; }
+
+// ws = nan_to_num(bf16(acc).to(fp16)): the bf16 GEMM output converted to fp16.
+__device__ __forceinline__ float ref_gemm_to_f16(float acc) { return nan_to_zero(round_f16(round_bf16(acc))); }
+
+// v_new (fp16 value) from u (bf16 value) and the MMA1 accumulator.
+__device__ __forceinline__ float ref_vnew(float u, float acc)
+{
+    return cast_f16(__fsub_rn(cast_f16(u), ref_gemm_to_f16(acc)));
+}
+
+// v_decay operand of MMA2: bf16(fp16(v_new * gate)).
+__device__ __forceinline__ float ref_vdecay(float vnew, float gate_f16)
+{
+    return round_bf16(cast_f16(__fmul_rn(vnew, gate_f16)));
+}
+
+// New bf16 state from the old bf16 state, alpha = fp16(exp(fp16(g_last))) and
+// the MMA2 accumulator: bf16(bf16(fp16(fp16(S) * alpha)) + bf16(fp16(bf16(acc)))).
+__device__ __forceinline__ float ref_state(float s, float alpha_f16, float acc)
+{
+    const float hd = cast_f16(__fmul_rn(cast_f16(s), alpha_f16));
+    const float up = ref_gemm_to_f16(acc);
+    return round_bf16(__fadd_rn(round_bf16(hd), round_bf16(up)));
+}
+
+// gate = fp16(exp(g_last - g)) (reference), alpha = fp16(exp(fp16(g_last))).
+__device__ __forceinline__ float ref_gate(float g_last, float g) { return cast_f16(expf(g_last - g)); }
+__device__ __forceinline__ float ref_alpha(float g_last) { return round_f16(expf(cast_f16(g_last))); }
+
+// Triton's safe_exp (docs/problem.txt:272-274).
+__device__ __forceinline__ float safe_exp(float x) { return expf(x <= 0.0f ? x : -INFINITY); }
+
+__device__ __forceinline__ float load_io(const void* base, int32_t dt, int64_t i)
+{
+    if (dt == kBF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(base)[i]);
+    return reinterpret_cast<const float*>(base)[i];
+}
+
+__device__ __forceinline__ void store_io(void* base, int32_t dt, int64_t i, float v)
+{
+    if (dt == kBF16)
+        reinterpret_cast<__nv_bfloat16*>(base)[i] = __float2bfloat16_rn(v);
+    else
+        reinterpret_cast<float*>(base)[i] = v;
+}
+
+}  // namespace cgdr

@@ -1,0 +1,495 @@
+// Tensor-core (tcgen05) kernel for sm_100a.
+//
+// One CTA owns one (sequence, value head, V tile of VT columns) and walks the
+// sequence's 64-token chunks in order -- the task split of the reference's
+// ProcessTask (op_kernel/chunk_gated_delta_rule_fwd_h.h:421-510), with the
+// state resident on chip instead of bounced through global memory.
+//
+// Warp roles (block = 32 * (4*EW + 2) threads):
+//   warps 0 .. 4*EW-1  epilogue: warp w reads TMEM lane quadrant w%4 and the
+//                      column slice (w/4) of width VT/EW;
+//   warp 4*EW          TMA producer: k_c, w_c, u_c of chunk c into a ring of
+//                      STAGES shared-memory stages;
+//   warp 4*EW+1        MMA issuer and TMEM owner.
+//
+// Per chunk c (S = state before the chunk, bf16 copy in shared memory):
+//   MMA1  D1[t,v] = sum_k w_c[t,k] S[k,v]        M=64, N=VT, K=K   (A K-major, B MN-major)
+//   epi1  v_new = u - D1 -> v_new tile (TMA store); v_dec = v_new*gate -> in place of u
+//   MMA2  D2[k,v] = sum_t k_c[t,k] v_dec[t,v]    M=K,  N=VT, K=64  (A, B MN-major)
+//   epi2  S = S*alpha + D2 (fp32 registers) -> bf16 S tile -> h[c+1] (TMA store)
+// All shared-memory tiles use the 128-byte swizzle, in 64-column (128 B)
+// sub-tiles, so one layout serves the TMA boxes and the UMMA descriptors.
+//
+// Every wait is bounded (WaitCtl); on expiry the CTA raises its abort flag,
+// records the role in the status word, drains its own copies and returns.
+#pragma once
+
+#include "common.cuh"
+#include "ptx.cuh"
+
+namespace cgdr {
+
+struct TcMaps {
+    CUtensorMap k;  // dims (K, HK, T, B), box (64, 1, 64, 1)
+    CUtensorMap w;  // dims (K, H, T, B),  box (64, 1, 64, 1)
+    CUtensorMap u;  // dims (V, H, T, B),  box (64, 1, 64, 1)
+    CUtensorMap v;  // dims (V, H, T, B),  box (64, 1, 16, 1)   (v_new store, 16 token rows)
+    CUtensorMap h;  // dims (V, K, H, NTdim, B), box (64, ROWS, 1, 1, 1)
+};
+
+struct TcArgs {
+    TcMaps maps;
+    FwdHParams p;
+};
+
+template <int K_, int VT, int STAGES, int EW>
+struct TcConfig {
+    static_assert(K_ == 64 || K_ == 128, "tensor-core path: K in {64, 128}");
+    static_assert(VT == 64 || VT == 128, "tensor-core path: V tile in {64, 128}");
+    static_assert(EW == 1 || EW == VT / 64, "column split must be 1 or one warp per 64-column sub-tile");
+    static constexpr int kEpiWarps = 4 * EW;
+    static constexpr int kThreads = 32 * (kEpiWarps + 2);
+    static constexpr int kProducerWarp = kEpiWarps;
+    static constexpr int kMmaWarp = kEpiWarps + 1;
+    static constexpr int kCW = VT / EW;                 // columns per epilogue warp
+    static constexpr int kSubK = K_ / 64;              // 64-column sub-tiles of k_c / w_c
+    static constexpr int kSubV = VT / 64;              // 64-column sub-tiles of u_c / S / v_new
+    static constexpr int kTileKBytes = K_ * 128;       // [64 tokens][K] bf16
+    static constexpr int kTileUBytes = VT * 128;       // [64 tokens][VT] bf16
+    static constexpr int kStageBytes = 2 * kTileKBytes + kTileUBytes;
+    static constexpr int kSBytes = K_ * VT * 2;        // [K][VT] bf16
+    static constexpr int kSSubBytes = K_ * 128;        // one 64-column sub-tile of S
+    static constexpr int kVoutBytes = 64 * VT * 2;
+    static constexpr int kOffS = STAGES * kStageBytes;
+    static constexpr int kOffVout = kOffS + kSBytes;
+    static constexpr int kOffBar = kOffVout + kVoutBytes;
+    static constexpr int kNumBars = 2 * STAGES + 5;
+    static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;  // + tmem slot, abort flag, alignment
+    static constexpr uint32_t kStageTx = kStageBytes;
+    static constexpr int kTmemCols = 2 * VT;            // D1 at [0, VT), D2 at [VT, 2VT)
+    static constexpr int kHRows = (K_ == 128) ? 32 : 16;  // S rows per warp quadrant
+    static constexpr int kMinBlocks = (VT == 64) ? 2 : 1;  // CTAs resident per SM the tile is sized for
+    static constexpr uint32_t kIdesc1 = umma_idesc_bf16(64, VT, false, true);
+    static constexpr uint32_t kIdesc2 = umma_idesc_bf16(K_, VT, true, true);
+};
+
+// Byte offset of element (row, col) inside a swizzled tile made of 64-column
+// sub-tiles of `sub_bytes` each (128-byte rows, 16-byte chunks XOR row%8).
+__device__ __forceinline__ uint32_t sw128_off(int row, int col, int sub_bytes)
+{
+    const int sub = col >> 6, cc = col & 63;
+    return sub * sub_bytes + row * 128 + ((((cc >> 3) ^ (row & 7)) & 7) << 4) + ((cc & 7) << 1);
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi)
+{
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__device__ __forceinline__ float2 unpack_bf16x2(uint32_t v)
+{
+    return make_float2(__uint_as_float(v << 16), __uint_as_float(v & 0xffff0000u));
+}
+
+template <int K_, int VT, int STAGES, int EW, bool REF>
+__global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConfig<K_, VT, STAGES, EW>::kMinBlocks)
+    fwd_h_tc_kernel(const __grid_constant__ TcArgs args)
+{
+    using Cfg = TcConfig<K_, VT, STAGES, EW>;
+    const FwdHParams& p = args.p;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBar);
+    uint64_t* full = bars;
+    uint64_t* empty = bars + STAGES;
+    uint64_t* mma1_done = bars + 2 * STAGES;
+    uint64_t* mma2_done = mma1_done + 1;
+    uint64_t* vdec_ready = mma1_done + 2;
+    uint64_t* s_ready = mma1_done + 3;
+    uint64_t* mma_drain = mma1_done + 4;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Cfg::kNumBars);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    volatile int* never_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);  // drains ignore aborts
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (p.status && (*reinterpret_cast<volatile int*>(p.status) & 0x2)) return;  // bad varlen metadata
+
+    int64_t n, hv, vt;
+    {
+        const int64_t bid = blockIdx.x;
+        vt = bid % p.n_vtiles;
+        const int64_t rest = bid / p.n_vtiles;
+        hv = rest % p.H;
+        const int64_t rank = rest / p.H;
+        n = (p.varlen && p.seq_order) ? p.seq_order[rank] : rank;
+    }
+    const SeqInfo si = seq_info(p, n);
+    const int64_t kh = hv / (p.H / p.HK);
+    const int v0 = static_cast<int>(vt * VT);
+    const int64_t nchunks = (si.len + kChunk - 1) / kChunk;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(mma1_done, 1);
+        mbar_init(mma2_done, 1);
+        mbar_init(vdec_ready, Cfg::kEpiWarps);
+        mbar_init(s_ready, Cfg::kEpiWarps);
+        mbar_init(mma_drain, 1);
+        *abort_flag = 0;
+        *never_flag = 0;
+        fence_mbarrier_init();
+    }
+    if (warp == Cfg::kMmaWarp) {
+        tmem_alloc(tmem_slot, Cfg::kTmemCols);
+        tmem_relinquish();
+    }
+    if (warp == Cfg::kProducerWarp && lane == 0) {
+        prefetch_tensormap(&args.maps.k);
+        prefetch_tensormap(&args.maps.w);
+        prefetch_tensormap(&args.maps.u);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const WaitCtl ctl{abort_flag, p.status, p.timeout_ns};
+    const uint32_t sbase = smem_u32(smem);
+
+    auto kc_addr = [&](int s) { return sbase + s * Cfg::kStageBytes; };
+    auto wc_addr = [&](int s) { return sbase + s * Cfg::kStageBytes + Cfg::kTileKBytes; };
+    auto uc_addr = [&](int s) { return sbase + s * Cfg::kStageBytes + 2 * Cfg::kTileKBytes; };
+
+    if (warp == Cfg::kProducerWarp) {
+        // ------------------------------------------------------------ producer
+        int64_t issued = 0;
+        if (lane == 0) {
+            for (int64_t c = 0; c < nchunks; ++c) {
+                const int s = static_cast<int>(c % STAGES);
+                const uint32_t use = static_cast<uint32_t>(c / STAGES);
+                if (c >= STAGES && !mbar_wait(&empty[s], (use - 1) & 1, ctl, 0x10)) break;
+                if (p.fault_inject && c == 1) break;  // test hook: consumers' waits must expire
+                mbar_arrive_expect_tx(&full[s], Cfg::kStageTx);
+                const int t0 = static_cast<int>(si.bos + c * kChunk);
+                const int b = static_cast<int>(si.b);
+#pragma unroll
+                for (int sub = 0; sub < Cfg::kSubK; ++sub)
+                    tma_load_4d(&args.maps.k, smem + s * Cfg::kStageBytes + sub * 8192, &full[s], sub * 64,
+                                static_cast<int>(kh), t0, b);
+#pragma unroll
+                for (int sub = 0; sub < Cfg::kSubK; ++sub)
+                    tma_load_4d(&args.maps.w, smem + s * Cfg::kStageBytes + Cfg::kTileKBytes + sub * 8192, &full[s],
+                                sub * 64, static_cast<int>(hv), t0, b);
+#pragma unroll
+                for (int sub = 0; sub < Cfg::kSubV; ++sub)
+                    tma_load_4d(&args.maps.u, smem + s * Cfg::kStageBytes + 2 * Cfg::kTileKBytes + sub * 8192,
+                                &full[s], v0 + sub * 64, static_cast<int>(hv), t0, b);
+                ++issued;
+            }
+            // Drain: never leave the CTA while a load may still land in its
+            // shared memory (bounded, and independent of the abort flag).
+            const int64_t first = issued > STAGES ? issued - STAGES : 0;
+            WaitCtl drain{never_flag, p.status, p.timeout_ns};
+            for (int64_t c = first; c < issued; ++c)
+                mbar_wait(&full[c % STAGES], static_cast<uint32_t>(c / STAGES) & 1, drain, 0x10);
+        }
+    } else if (warp == Cfg::kMmaWarp) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            const uint32_t d1 = tmem;
+            const uint32_t d2 = tmem + VT;
+            const uint32_t s_addr = sbase + Cfg::kOffS;
+            for (int64_t c = 0; c < nchunks; ++c) {
+                const int s = static_cast<int>(c % STAGES);
+                if (!mbar_wait(&full[s], static_cast<uint32_t>(c / STAGES) & 1, ctl, 0x20)) break;
+                if (!mbar_wait(s_ready, static_cast<uint32_t>(c) & 1, ctl, 0x20)) break;
+                tc_fence_after();
+#pragma unroll
+                for (int kk = 0; kk < K_ / 16; ++kk) {
+                    const uint64_t a = umma_desc_sw128(wc_addr(s) + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024);
+                    const uint64_t bdesc = umma_desc_sw128(s_addr + kk * 2048, Cfg::kSSubBytes, 1024);
+                    tc_mma_bf16(d1, a, bdesc, Cfg::kIdesc1, kk > 0 ? 1u : 0u);
+                }
+                tc_commit(mma1_done);
+                if (!mbar_wait(vdec_ready, static_cast<uint32_t>(c) & 1, ctl, 0x20)) break;
+                tc_fence_after();
+#pragma unroll
+                for (int tt = 0; tt < 4; ++tt) {
+                    const uint64_t a = umma_desc_sw128(kc_addr(s) + tt * 2048, 8192, 1024);
+                    const uint64_t bdesc = umma_desc_sw128(uc_addr(s) + tt * 2048, 8192, 1024);
+                    tc_mma_bf16(d2, a, bdesc, Cfg::kIdesc2, tt > 0 ? 1u : 0u);
+                }
+                tc_commit(mma2_done);
+                tc_commit(&empty[s]);
+            }
+            // Drain: every MMA this thread issued has completed before the
+            // TMEM it writes is released (matters only on an abort path).
+            tc_commit(mma_drain);
+            WaitCtl drain{never_flag, p.status, p.timeout_ns};
+            mbar_wait(mma_drain, 0, drain, 0x20);
+        }
+    } else {
+        // ------------------------------------------------------------ epilogue
+        const int q = warp & 3;          // TMEM lane quadrant
+        const int e = warp >> 2;         // column slice
+        const int cbase = e * Cfg::kCW;  // first column (within the V tile) of this warp
+        const bool ref = REF;
+        uint8_t* s_tile = smem + Cfg::kOffS;
+        uint8_t* vout = smem + Cfg::kOffVout;
+        const int ta = 16 * q + (lane >> 2);  // epi1 token rows ta, ta+8
+        const int tb = ta + 8;
+        const int pc = 2 * (lane & 3);        // column pair offset inside an 8-column group
+
+        // State rows owned by this thread (epi2 fragment):
+        //   K=128: row 32q+lane, columns cbase + [0, CW)
+        //   K=64 : rows 16q+lane/4 (+8), columns cbase + 8j + pc + {0,1}
+        constexpr int kNState = (K_ == 128) ? Cfg::kCW : Cfg::kCW / 2;
+        float st[kNState];
+        auto st_row_col = [&](int i, int& row, int& col) {
+            if constexpr (K_ == 128) {
+                row = 32 * q + lane;
+                col = cbase + i;
+            } else {
+                // i = 4*j8 + 2*half + bit: j8 = 8-column group, half selects row +8
+                const int j8 = i >> 2, half = (i >> 1) & 1, bit = i & 1;
+                row = 16 * q + (lane >> 2) + 8 * half;
+                col = cbase + 8 * j8 + pc + bit;
+            }
+        };
+
+        // ---- initial state
+#pragma unroll
+        for (int i = 0; i < kNState; ++i) {
+            int row, col;
+            st_row_col(i, row, col);
+            float x = 0.0f;
+            if (p.h0)
+                x = load_io(p.h0, p.h0_dtype, si.n * p.h0_sn + hv * p.h0_sh + row * p.h0_sk + v0 + col);
+            st[i] = ref ? round_bf16(x) : x;
+        }
+        auto write_state_tile = [&]() {
+            if constexpr (K_ == 128) {
+                const int row = 32 * q + lane;
+#pragma unroll
+                for (int j = 0; j < Cfg::kCW / 8; ++j) {
+                    uint4 v;
+                    v.x = pack_bf16x2(st[8 * j + 0], st[8 * j + 1]);
+                    v.y = pack_bf16x2(st[8 * j + 2], st[8 * j + 3]);
+                    v.z = pack_bf16x2(st[8 * j + 4], st[8 * j + 5]);
+                    v.w = pack_bf16x2(st[8 * j + 6], st[8 * j + 7]);
+                    *reinterpret_cast<uint4*>(s_tile + sw128_off(row, cbase + 8 * j, Cfg::kSSubBytes)) = v;
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < kNState; i += 2) {
+                    int row, col;
+                    st_row_col(i, row, col);
+                    *reinterpret_cast<uint32_t*>(s_tile + sw128_off(row, col, Cfg::kSSubBytes)) =
+                        pack_bf16x2(st[i], st[i + 1]);
+                }
+            }
+        };
+        auto store_h = [&](int64_t chunk) {
+            // this warp's rows of its sub-tiles -> h[b, boh+chunk, hv, rows, cols]
+            if (lane == 0) {
+#pragma unroll
+                for (int sub = 0; sub < Cfg::kSubV; ++sub) {
+                    if (sub * 64 < cbase || sub * 64 >= cbase + Cfg::kCW) continue;
+                    tma_store_5d(&args.maps.h, s_tile + sub * Cfg::kSSubBytes + Cfg::kHRows * q * 128, v0 + sub * 64,
+                                 Cfg::kHRows * q, static_cast<int>(hv), static_cast<int>(si.boh + chunk),
+                                 static_cast<int>(si.b));
+                }
+                bulk_commit_group();
+            }
+        };
+
+        bool ok = true;
+        write_state_tile();
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (nchunks > 0) store_h(0);
+        if (lane == 0) mbar_arrive(s_ready);
+
+        // gate inputs of the current chunk (prefetched one chunk ahead)
+        const int64_t gbase = si.b * p.g_sb + hv * p.g_sh;
+        auto g_at = [&](int64_t t) -> float { return p.g ? __ldg(p.g + gbase + t * p.g_st) : 0.0f; };
+        float g_a = 0.f, g_b = 0.f, g_l = 0.f;
+        if (nchunks > 0) {
+            const int len0 = static_cast<int>(si.len < kChunk ? si.len : kChunk);
+            g_l = g_at(si.bos + len0 - 1);
+            g_a = ta < len0 ? g_at(si.bos + ta) : g_l;
+            g_b = tb < len0 ? g_at(si.bos + tb) : g_l;
+        }
+
+        for (int64_t c = 0; c < nchunks && ok; ++c) {
+            const int s = static_cast<int>(c % STAGES);
+            const int64_t t0 = si.bos + c * kChunk;
+            const int len = static_cast<int>(si.len - c * kChunk < kChunk ? si.len - c * kChunk : kChunk);
+            const bool partial_varlen = p.varlen && len < kChunk;
+
+            // ================= epilogue 1 =================
+            if (!mbar_wait(mma1_done, static_cast<uint32_t>(c) & 1, ctl, 0x40)) { ok = false; break; }
+            if (!mbar_wait(&full[s], static_cast<uint32_t>(c / STAGES) & 1, ctl, 0x40)) { ok = false; break; }
+            tc_fence_after();
+            uint32_t acc[Cfg::kCW / 32][16];
+#pragma unroll
+            for (int cb = 0; cb < Cfg::kCW / 32; ++cb)
+                tmem_ld_16x256b_x4(tmem + ((32u * q) << 16) + static_cast<uint32_t>(cbase + 32 * cb), acc[cb]);
+            tmem_wait_ld();
+            if (lane == 0) bulk_wait_group_read0();  // v_new staging / S no longer read by old stores
+            __syncwarp();
+
+            float gate_a, gate_b, alpha;
+            if (ref) {
+                gate_a = ref_gate(g_l, g_a);
+                gate_b = ref_gate(g_l, g_b);
+                alpha = ref_alpha(g_l);
+            } else if (p.use_g) {
+                gate_a = safe_exp(g_l - g_a);
+                gate_b = safe_exp(g_l - g_b);
+                alpha = expf(g_l);
+            } else {
+                gate_a = gate_b = alpha = 1.0f;
+            }
+            uint8_t* ut = smem + s * Cfg::kStageBytes + 2 * Cfg::kTileKBytes;
+#pragma unroll
+            for (int cb = 0; cb < Cfg::kCW / 32; ++cb) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int col = cbase + 32 * cb + 8 * j + pc;
+#pragma unroll
+                    for (int half = 0; half < 2; ++half) {
+                        const int t = half ? tb : ta;
+                        const float gt = half ? gate_b : gate_a;
+                        const float a0 = __uint_as_float(acc[cb][4 * j + 2 * half + 0]);
+                        const float a1 = __uint_as_float(acc[cb][4 * j + 2 * half + 1]);
+                        const uint32_t off = sw128_off(t, col, 8192);
+                        uint32_t vd = 0, vo = 0;
+                        if (t < len) {
+                            const float2 uu = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(ut + off));
+                            float vn0, vn1, d0, d1;
+                            if (ref) {
+                                vn0 = ref_vnew(uu.x, a0);
+                                vn1 = ref_vnew(uu.y, a1);
+                                d0 = ref_vdecay(vn0, gt);
+                                d1 = ref_vdecay(vn1, gt);
+                            } else {
+                                vn0 = uu.x - a0;
+                                vn1 = uu.y - a1;
+                                d0 = vn0 * gt;
+                                d1 = vn1 * gt;
+                            }
+                            vo = pack_bf16x2(vn0, vn1);
+                            vd = pack_bf16x2(d0, d1);
+                            if (partial_varlen && p.v_new) {
+                                const int64_t vi = si.b * p.v_sb + (t0 + t) * p.v_st + hv * p.v_sh + v0 + col;
+                                *reinterpret_cast<uint32_t*>(reinterpret_cast<__nv_bfloat16*>(p.v_new) + vi) = vo;
+                            }
+                        }
+                        *reinterpret_cast<uint32_t*>(ut + off) = vd;
+                        *reinterpret_cast<uint32_t*>(vout + off) = vo;
+                    }
+                }
+            }
+            // prefetch next chunk's gate inputs
+            if (c + 1 < nchunks) {
+                const int64_t tn = t0 + kChunk;
+                const int lenn =
+                    static_cast<int>(si.len - (c + 1) * kChunk < kChunk ? si.len - (c + 1) * kChunk : kChunk);
+                g_l = g_at(tn + lenn - 1);
+                g_a = ta < lenn ? g_at(tn + ta) : g_l;
+                g_b = tb < lenn ? g_at(tn + tb) : g_l;
+            }
+            fence_proxy_async_smem();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(vdec_ready);
+                if (p.v_new && !partial_varlen) {
+#pragma unroll
+                    for (int sub = 0; sub < Cfg::kSubV; ++sub) {
+                        if (sub * 64 < cbase || sub * 64 >= cbase + Cfg::kCW) continue;
+                        tma_store_4d(&args.maps.v, vout + sub * 8192 + 16 * q * 128, v0 + sub * 64,
+                                     static_cast<int>(hv), static_cast<int>(t0 + 16 * q), static_cast<int>(si.b));
+                    }
+                    bulk_commit_group();
+                }
+            }
+
+            // ================= epilogue 2 =================
+            if (!mbar_wait(mma2_done, static_cast<uint32_t>(c) & 1, ctl, 0x40)) { ok = false; break; }
+            tc_fence_after();
+            const bool more = c + 1 < nchunks;
+            if (lane == 0 && more) bulk_wait_group_read0();
+            __syncwarp();
+            if constexpr (K_ == 128) {
+#pragma unroll
+                for (int cb = 0; cb < Cfg::kCW / 32; ++cb) {
+                    uint32_t r0[16], r1[16];
+                    const uint32_t ta2 = tmem + VT + ((32u * q) << 16) + static_cast<uint32_t>(cbase + 32 * cb);
+                    tmem_ld_32x32b_x16(ta2, r0);
+                    tmem_ld_32x32b_x16(ta2 + 16, r1);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        float& s0 = st[32 * cb + i];
+                        float& s1 = st[32 * cb + 16 + i];
+                        if (ref) {
+                            s0 = ref_state(s0, alpha, __uint_as_float(r0[i]));
+                            s1 = ref_state(s1, alpha, __uint_as_float(r1[i]));
+                        } else {
+                            s0 = fmaf(s0, alpha, __uint_as_float(r0[i]));
+                            s1 = fmaf(s1, alpha, __uint_as_float(r1[i]));
+                        }
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int cb = 0; cb < Cfg::kCW / 32; ++cb) {
+                    uint32_t r[16];
+                    tmem_ld_16x256b_x4(tmem + VT + ((32u * q) << 16) + static_cast<uint32_t>(cbase + 32 * cb), r);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        float& sv = st[16 * cb + i];
+                        sv = ref ? ref_state(sv, alpha, __uint_as_float(r[i])) : fmaf(sv, alpha, __uint_as_float(r[i]));
+                    }
+                }
+            }
+            if (more) {
+                write_state_tile();
+                fence_proxy_async_smem();
+                tc_fence_before();
+                __syncwarp();
+                store_h(c + 1);
+                if (lane == 0) mbar_arrive(s_ready);
+            } else {
+                tc_fence_before();
+            }
+        }
+        // ---- final state (plain stores; once per task)
+        if (ok && p.final_state) {
+#pragma unroll
+            for (int i = 0; i < kNState; ++i) {
+                int row, col;
+                st_row_col(i, row, col);
+                store_io(p.final_state, p.f_dtype, si.n * p.f_sn + hv * p.f_sh + row * p.f_sk + v0 + col, st[i]);
+            }
+        }
+        if (lane == 0) bulk_wait_group0();
+        __syncwarp();
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == Cfg::kMmaWarp) tmem_dealloc(tmem, Cfg::kTmemCols);
+}
+
+}  // namespace cgdr
