@@ -1,0 +1,250 @@
+"""C-ABI surface on CPU (no kernel is launched): the library loads, exports
+every symbol include/cgdr_fwd_h.h declares, and phase 1 validates and plans
+exactly as the reference's host code does.
+
+The accept/reject cases port the reference's InferShape unit tests
+(code/tests/ut/op_host/test_chunk_gated_delta_rule_fwd_h_infershape.cpp:113-222)
+and the plan checks port its tiling tests
+(code/tests/ut/op_host/test_chunk_gated_delta_rule_fwd_h_tiling.cpp:39-162).
+Phase 1 only reads shapes, strides and dtypes, so host tensors stand in for
+device buffers here.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+import cann_operator_challenge_august_b200 as cg
+from cann_operator_challenge_august_b200 import _lib
+
+ROOT = Path(__file__).resolve().parents[1]
+BF, F32, I64 = torch.bfloat16, torch.float32, torch.int64
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    lib = _lib.load()
+    header = (ROOT / "include" / "cgdr_fwd_h.h").read_text()
+    declared = set(re.findall(r"^(?:cgdrStatus|void|int32_t|const char\*)\s+(cgdr\w+)\(", header, re.MULTILINE))
+    assert declared == set(_lib.EXPORTS), declared ^ set(_lib.EXPORTS)
+    for sym in declared:
+        assert hasattr(lib, sym), sym
+    assert lib.cgdrGetAbiVersion() == 1
+
+
+def e(shape, dtype=BF):
+    return torch.empty(shape, dtype=dtype)
+
+
+def varlen_case(with_state=True, with_final=True, chunk=64):
+    """MakeVarlenCase of the reference UT: T=10016, N=2, NT=158, HV=8, HK=2, D=128."""
+    d = dict(k=e((1, 10016, 2, 128)), w=e((1, 8, 10016, 128)), u=e((1, 8, 10016, 128)),
+             g=e((1, 8, 10016), F32), initial_state=e((2, 8, 128, 128)) if with_state else None,
+             cu_seqlens=e((3,), I64), chunk_indices=e((158, 2), I64), chunk_size=chunk,
+             h=e((1, 8, 158, 128, 128)), v=e((1, 8, 10016, 128)),
+             final_state=e((2, 8, 128, 128)) if with_final else None)
+    return d
+
+
+def fixed_case():
+    """MakeFixedLengthCase: T=65, HV=4, HK=2, D=64."""
+    return dict(k=e((1, 65, 2, 64)), w=e((1, 4, 65, 64)), u=e((1, 4, 65, 64)), g=e((1, 4, 65), F32),
+                initial_state=e((1, 4, 64, 64)), cu_seqlens=None, chunk_indices=None, chunk_size=64,
+                h=e((1, 4, 2, 64, 64)), v=e((1, 4, 65, 64)), final_state=e((1, 4, 64, 64)))
+
+
+def phase1(d, strict=True, **kw):
+    return cg.ChunkGatedDeltaRuleFwdH(d["k"], d["w"], d["u"], d["g"], d["initial_state"], d["cu_seqlens"],
+                                      d["chunk_indices"], d["chunk_size"], d["h"], d["v"], d["final_state"],
+                                      strict_reference_limits=strict, **kw)
+
+
+def reject(d, status, strict=True, **kw):
+    with pytest.raises(cg.CgdrValueError) as ei:
+        phase1(d, strict=strict, **kw)
+    assert ei.value.status_name == status, str(ei.value)
+
+
+# ---- InferShape UT ports --------------------------------------------------------
+
+def test_varlen_success():
+    op = phase1(varlen_case())
+    pl = op.plan
+    assert (pl["batch"], pl["value_heads"], pl["chunk_count"], pl["key_dim"], pl["value_dim"]) == (1, 8, 158, 128, 128)
+    assert pl["sequence_count"] == 2
+
+
+def test_optional_initial_state_and_final_state():
+    op = phase1(varlen_case(False, False))
+    assert op.plan["has_initial_state"] == 0 and op.plan["store_final_state"] == 0
+
+
+def test_fixed_length_success():
+    op = phase1(fixed_case())
+    assert op.plan["chunk_count"] == 2 and op.plan["sequence_count"] == 1
+
+
+def test_rejects_invalid_batch():
+    d = varlen_case()
+    d["k"] = e((2, 10016, 2, 128))
+    with pytest.raises(cg.CgdrValueError):
+        phase1(d)
+
+
+def test_rejects_invalid_rank():
+    d = varlen_case()
+    d["g"] = e((1, 8, 10016, 1), F32)
+    reject(d, "BAD_RANK")
+
+
+def test_rejects_mismatched_key_and_value_dimensions():
+    d = varlen_case()
+    d["u"] = e((1, 8, 10016, 64))
+    with pytest.raises(cg.CgdrValueError):
+        phase1(d)
+
+
+def test_rejects_out_of_range_head_dimension():
+    d = varlen_case()
+    d["k"], d["w"], d["u"] = e((1, 10016, 2, 16)), e((1, 8, 10016, 16)), e((1, 8, 10016, 16))
+    d["initial_state"] = e((2, 8, 16, 16))
+    d["h"], d["v"], d["final_state"] = e((1, 8, 158, 16, 16)), e((1, 8, 10016, 16)), e((2, 8, 16, 16))
+    reject(d, "BAD_SHAPE")
+    # outside the reference's limits this build still accepts K = V = 16 (general kernel)
+    assert phase1(d, strict=False).plan["kernel"] == 2
+
+
+def test_rejects_non_divisible_head_ratio():
+    d = varlen_case()
+    d["w"], d["u"], d["g"] = e((1, 7, 10016, 128)), e((1, 7, 10016, 128)), e((1, 7, 10016), F32)
+    d["initial_state"] = e((2, 7, 128, 128))
+    d["h"], d["v"], d["final_state"] = e((1, 7, 158, 128, 128)), e((1, 7, 10016, 128)), e((2, 7, 128, 128))
+    reject(d, "BAD_SHAPE")
+
+
+def test_rejects_mismatched_token_dimension():
+    d = varlen_case()
+    d["w"] = e((1, 8, 10015, 128))
+    reject(d, "BAD_SHAPE")
+
+
+def test_rejects_invalid_initial_state():
+    d = varlen_case()
+    d["initial_state"] = e((1, 8, 128, 128))
+    reject(d, "BAD_SHAPE")
+
+
+def test_rejects_invalid_chunk_indices_shape():
+    d = varlen_case()
+    d["chunk_indices"] = e((158, 3), I64)
+    reject(d, "BAD_VARLEN")
+
+
+def test_rejects_impossible_chunk_count():
+    d = varlen_case()
+    d["chunk_indices"] = e((160, 2), I64)
+    d["h"] = e((1, 8, 160, 128, 128))
+    reject(d, "BAD_VARLEN")
+
+
+def test_rejects_half_input():
+    d = varlen_case()
+    d["k"] = e((1, 10016, 2, 128), torch.float16)
+    reject(d, "BAD_DTYPE")
+
+
+def test_rejects_unsupported_chunk_size():
+    reject(varlen_case(chunk=32), "BAD_CHUNK_SIZE")
+
+
+def test_rejects_only_one_varlen_metadata_input():
+    d = varlen_case()
+    d["chunk_indices"] = None
+    reject(d, "BAD_VARLEN")
+    reject(d, "BAD_VARLEN", extended=False)
+
+
+def test_strict_limits_reject_what_the_reference_rejects():
+    d = varlen_case()
+    d["cu_seqlens"] = e((6,), I64)  # five sequences > the reference's four
+    d["initial_state"] = e((5, 8, 128, 128))
+    d["final_state"] = e((5, 8, 128, 128))
+    reject(d, "BAD_VARLEN")
+    assert phase1(d, strict=False).plan["sequence_count"] == 5
+
+
+# ---- tiling UT ports ------------------------------------------------------------
+
+def test_plan_varlen_all_optional_paths():
+    pl = phase1(varlen_case()).plan
+    assert pl["plan_key"] == 7  # has_init | varlen<<1 | store_final<<2 (tiling.cpp:255-259)
+    assert (pl["total_tokens"], pl["sequence_count"], pl["chunk_count"]) == (10016, 2, 158)
+    assert (pl["value_heads"], pl["key_heads"], pl["head_ratio"]) == (8, 2, 4)
+    assert pl["kernel"] == 1 and pl["v_tile"] in (64, 128)
+    assert pl["task_count"] == 2 * 8 * pl["v_tile_count"] == pl["grid"]
+    assert pl["workspace_bytes"] >= 256 + 4 * 3 + 4 * 2
+
+
+def test_plan_fixed_length_without_optional_state_or_final():
+    d = fixed_case()
+    d["initial_state"] = None
+    d["final_state"] = None
+    pl = phase1(d).plan
+    assert pl["plan_key"] == 0
+    assert (pl["sequence_count"], pl["chunk_count"], pl["task_count"]) == (1, 2, 4 * pl["v_tile_count"])
+    assert pl["workspace_bytes"] == 256
+
+
+def test_plan_rejects_half_present_varlen_metadata():
+    d = dict(k=e((1, 64, 1, 64)), w=e((1, 1, 64, 64)), u=e((1, 1, 64, 64)), g=e((1, 1, 64), F32),
+             initial_state=None, cu_seqlens=e((2,), I64), chunk_indices=None, chunk_size=64,
+             h=e((1, 1, 1, 64, 64)), v=e((1, 1, 64, 64)), final_state=None)
+    reject(d, "BAD_VARLEN", extended=False)
+
+
+def test_plan_kernel_selection():
+    """bf16 with K in {64, 128} and V % 64 == 0 -> tensor cores; else general."""
+    B, T, H = 4, 8192, 32
+    k, w, u, g = e((B, T, H, 128)), e((B, T, H, 128)), e((B, T, H, 128)), e((B, T, H), F32)
+    h, v, f = e((B, 128, H, 128, 128)), e((B, T, H, 128)), e((B, H, 128, 128), F32)
+    op = cg.ChunkGatedDeltaRuleFwdH(k, w, u, g, None, None, None, 64, h, v, f, layout="token_major",
+                                    numerics="fp32_state")
+    pl = op.plan
+    assert pl["kernel"] == 1 and pl["grid"] == pl["task_count"] == B * H * (128 // pl["v_tile"])
+    # fp32 I/O -> general kernel
+    k32, w32, u32 = e((1, 256, 2, 64), F32), e((1, 256, 2, 64), F32), e((1, 256, 2, 64), F32)
+    op = cg.ChunkGatedDeltaRuleFwdH(k32, w32, u32, e((1, 256, 2), F32), None, None, None, 64,
+                                    e((1, 4, 2, 64, 64), F32), e((1, 256, 2, 64), F32), e((1, 2, 64, 64), F32),
+                                    layout="token_major", numerics="fp32_state")
+    assert op.plan["kernel"] == 2
+    # fp32 I/O is not the reference arithmetic
+    with pytest.raises(cg.CgdrValueError):
+        cg.ChunkGatedDeltaRuleFwdH(k32, w32, u32, e((1, 256, 2), F32), None, None, None, 64,
+                                   e((1, 4, 2, 64, 64), F32), e((1, 256, 2, 64), F32), None,
+                                   layout="token_major", numerics="reference")
+
+
+def test_executor_lifecycle_and_errors():
+    lib = _lib.load()
+    op = phase1(fixed_case())
+    ex = op._ex
+    op._ex = None
+    lib.cgdrDestroyExecutor(ex)
+    st = lib.cgdrChunkGatedDeltaRuleFwdH(ctypes.c_void_p(1 << 20), 256, ctypes.c_void_p(0), ctypes.c_void_p(0))
+    assert _lib.STATUS_NAMES[st] == "BAD_EXECUTOR"
+    # a too-small workspace is refused before any device work
+    op = phase1(varlen_case())
+    ex = op._ex
+    op._ex = None
+    st = lib.cgdrChunkGatedDeltaRuleFwdH(ctypes.c_void_p(1 << 20), 16, ex, ctypes.c_void_p(0))
+    assert _lib.STATUS_NAMES[st] == "WORKSPACE_TOO_SMALL"
+
+
+def test_python_front_end_refuses_cpu_tensors():
+    k = torch.zeros(1, 64, 1, 64, dtype=BF)
+    with pytest.raises(ValueError, match="CUDA"):
+        cg.chunk_gated_delta_rule_fwd_h(k, k, k, torch.zeros(1, 64, 1))
