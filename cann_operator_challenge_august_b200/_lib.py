@@ -28,6 +28,8 @@ DT_BF16, DT_FLOAT32, DT_FLOAT16, DT_INT64, DT_INT32 = 1, 2, 3, 4, 5
 LAYOUT_HEAD_MAJOR, LAYOUT_TOKEN_MAJOR = 0, 1
 NUMERICS = {"reference": 0, "fp32_state": 1}
 
+NOALLOC_SCRATCH_BYTES = 65536  # CGDR_NOALLOC_SCRATCH_BYTES
+
 DEVICE_WAIT_TIMEOUT = 0x1
 DEVICE_BAD_VARLEN = 0x2
 
@@ -36,6 +38,7 @@ EXPORTS = (
     "cgdrChunkGatedDeltaRuleFwdHGetWorkspaceSize",
     "cgdrChunkGatedDeltaRuleFwdHGetWorkspaceSizeEx",
     "cgdrChunkGatedDeltaRuleFwdH",
+    "cgdrChunkGatedDeltaRuleFwdHNoAlloc",
     "cgdrDestroyExecutor",
     "cgdrGetPlan",
     "cgdrReadDeviceStatus",
@@ -103,6 +106,9 @@ def load() -> ctypes.CDLL:
     lib.cgdrChunkGatedDeltaRuleFwdHGetWorkspaceSizeEx.restype = ctypes.c_int
     lib.cgdrChunkGatedDeltaRuleFwdH.argtypes = [ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p, ctypes.c_void_p]
     lib.cgdrChunkGatedDeltaRuleFwdH.restype = ctypes.c_int
+    lib.cgdrChunkGatedDeltaRuleFwdHNoAlloc.argtypes = [ctypes.c_void_p, ctypes.c_void_p,
+                                                       ctypes.POINTER(ctypes.c_int32)]
+    lib.cgdrChunkGatedDeltaRuleFwdHNoAlloc.restype = ctypes.c_int
     lib.cgdrDestroyExecutor.argtypes = [ctypes.c_void_p]
     lib.cgdrDestroyExecutor.restype = None
     lib.cgdrGetPlan.argtypes = [ctypes.c_void_p, ctypes.POINTER(CgdrFwdHPlan)]

@@ -578,3 +578,59 @@ const char* cgdrGetLastErrorMessage(void) { return g_err; }
 int32_t cgdrGetAbiVersion(void) { return CGDR_ABI_VERSION; }
 
 }  // extern "C"
+
+// ---- phase 2 without allocation ------------------------------------------------------
+// The workspace of cgdrChunkGatedDeltaRuleFwdHNoAlloc: one file-scope device
+// array per GPU that loads the library.  Host code must not pass the symbol
+// itself to a kernel (on the host it is only a stand-in); its device address
+// comes from cudaGetSymbolAddress, looked up once per device.
+
+#include <mutex>
+
+namespace {
+
+__device__ __align__(256) uint8_t g_noalloc_scratch[CGDR_NOALLOC_SCRATCH_BYTES];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mutex;
+void* g_noalloc_addr[kMaxDevices] = {};
+
+}  // namespace
+
+extern "C" cgdrStatus cgdrChunkGatedDeltaRuleFwdHNoAlloc(cgdrExecutor* executor, void* stream,
+                                                        int32_t* device_status)
+{
+    if (!executor || executor->magic != kMagic) return fail(CGDR_STATUS_BAD_EXECUTOR, "invalid executor");
+    if (executor->plan.workspace_bytes > CGDR_NOALLOC_SCRATCH_BYTES) {
+        const unsigned long long need = executor->plan.workspace_bytes;
+        cgdrDestroyExecutor(executor);
+        return fail(CGDR_STATUS_WORKSPACE_TOO_SMALL,
+                    "this call needs %llu bytes of scratch; the built-in buffer holds %d "
+                    "(use cgdrChunkGatedDeltaRuleFwdH with a caller workspace)",
+                    need, CGDR_NOALLOC_SCRATCH_BYTES);
+    }
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+        cgdrDestroyExecutor(executor);
+        return fail(CGDR_STATUS_CUDA_ERROR, "cudaGetDevice: %s", cudaGetErrorString(e));
+    }
+    void* scratch = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+        if (!g_noalloc_addr[dev]) {
+            void* addr = nullptr;
+            e = cudaGetSymbolAddress(&addr, g_noalloc_scratch);
+            if (e != cudaSuccess || addr == nullptr) {
+                cgdrDestroyExecutor(executor);
+                return fail(CGDR_STATUS_CUDA_ERROR, "cudaGetSymbolAddress(scratch): %s", cudaGetErrorString(e));
+            }
+            g_noalloc_addr[dev] = addr;
+        }
+        scratch = g_noalloc_addr[dev];
+    }
+    // The ordinary phase 2 on the built-in buffer (it clears the status word).
+    const cgdrStatus st = cgdrChunkGatedDeltaRuleFwdH(scratch, CGDR_NOALLOC_SCRATCH_BYTES, executor, stream);
+    if (st != CGDR_STATUS_SUCCESS || device_status == nullptr) return st;
+    return cgdrReadDeviceStatus(scratch, CGDR_NOALLOC_SCRATCH_BYTES, stream, device_status);
+}

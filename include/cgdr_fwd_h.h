@@ -193,6 +193,40 @@ cgdrStatus cgdrReadDeviceStatus(const void* workspace, uint64_t workspace_size, 
 #define CGDR_DEVICE_TIMEOUT_MMA 0x20
 #define CGDR_DEVICE_TIMEOUT_EPILOGUE 0x40
 
+/* Phase 2 without any allocation.  This entry point has no counterpart in
+ * the reference (its ACLNN API always returns a workspace size for the
+ * caller to allocate).
+ *
+ * It exists for callers that cannot call cudaMalloc: a plugin or library
+ * host that is handed only input/output pointers and a stream while its
+ * framework's memory pool owns the device memory (an inference server that
+ * reserves almost all HBM for its KV cache up front, for example), or a
+ * latency-critical path that must not trigger cudaMalloc's implicit
+ * device-wide synchronisation.  Instead of a caller workspace it uses a
+ * scratch buffer compiled into this library: a file-scope __device__ array
+ * of CGDR_NOALLOC_SCRATCH_BYTES (64 KiB) that every GPU which loads the
+ * library holds until the process exits.  Nothing here allocates: no
+ * cudaMalloc, no cudaFree, no allocating library routine.
+ *
+ * - Limit: a plan whose workspace exceeds CGDR_NOALLOC_SCRATCH_BYTES is
+ *   rejected with CGDR_STATUS_WORKSPACE_TOO_SMALL before any device work
+ *   (fixed-length inputs need 256 bytes; variable-length inputs need about
+ *   8 bytes per sequence, so up to roughly 8000 sequences fit).
+ * - Device: the buffer of the current device is used; `stream` must belong
+ *   to it.  The first call on each device looks up the buffer's address
+ *   (cudaGetSymbolAddress) with that device current; make that first call
+ *   before any stream capture.
+ * - Sharing: every call shares the one buffer, which keeps the last call's
+ *   contents; each call clears its status word before its kernels run.
+ *   Calls whose work overlaps on the GPU (other streams, other host
+ *   threads) race on the buffer: serialise them, e.g. on one stream.
+ * - `executor` is consumed whatever the outcome.  If `device_status` is not
+ *   NULL the call synchronises `stream` and stores the kernels' status word
+ *   there (0 = clean), returning CGDR_STATUS_DEVICE_ERROR when it is not 0;
+ *   with NULL the call stays asynchronous. */
+#define CGDR_NOALLOC_SCRATCH_BYTES 65536
+cgdrStatus cgdrChunkGatedDeltaRuleFwdHNoAlloc(cgdrExecutor* executor, void* stream, int32_t* device_status);
+
 /* Thread-local message describing the last failure on this thread. */
 const char* cgdrGetLastErrorMessage(void);
 
