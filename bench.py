@@ -48,6 +48,8 @@ CONFIGS = {
     "c5": dict(B=8, T=8192, H=64, HK=64, K=128, V=256, scaling="strong"),
     "c2": dict(B=2, T=4096, H=16, HK=16, K=128, V=128, scaling="weak"),
     "c3": dict(B=1, T=65536, H=32, HK=32, K=128, V=128, scaling="weak", h0=False),
+    # a quarter of the north-star workload (one sequence per head): the small case of ncu captures
+    "nsq": dict(B=1, T=8192, H=32, HK=32, K=128, V=128, scaling="weak"),
 }
 
 
@@ -74,14 +76,19 @@ def load_peaks():
     return 6650.0, "fallback"
 
 
-def load_traffic(config):
-    """dram bytes per launch from the committed ncu summary, if any."""
-    p = ROOT / "profiles" / f"traffic_{config}.json"
-    if p.exists():
-        try:
-            return json.loads(p.read_text())
-        except Exception:
-            return None
+def load_traffic(config, kernel):
+    """DRAM bytes per launch of `kernel` on `config`, from the committed ncu
+    summary profiles/traffic.txt (lines "config kernel bytes"), or None."""
+    p = ROOT / "profiles" / "traffic.txt"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        parts = line.split()
+        if len(parts) >= 3 and parts[0] == config and parts[1] == kernel:
+            try:
+                return float(parts[2])
+            except ValueError:
+                return None
     return None
 
 
@@ -277,6 +284,16 @@ def run_reference_arm(args, cfg_name, c, world, rank):
     return 0
 
 
+def _plan_outputs(inp, c, dev):
+    """Output tensors shaped for the phase-1 plan query (never launched)."""
+    import torch
+    B, T, H, K, V = c["B"], c["T"], c["H"], c["K"], c["V"]
+    NT = (T + 63) // 64
+    return (torch.empty(B, NT, H, K, V, dtype=torch.bfloat16, device=dev),
+            torch.empty(B, T, H, V, dtype=torch.bfloat16, device=dev),
+            torch.empty(B, H, K, V, dtype=torch.float32, device=dev))
+
+
 def config_block(name, c, world):
     return {
         "workload": f"{name}: chunk_gated_delta_rule_fwd_h bf16 B={c['B']} T={c['T']} H={c['H']} "
@@ -373,23 +390,28 @@ def main() -> int:
         for dst, src in zip(host_out, o):
             dst.copy_(src, non_blocking=True)
 
-    e2e_step()
-    torch.cuda.synchronize()
-    barrier(world)
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.e2e_steps):
+    e2e_ms = e2e_value = None
+    if args.e2e_steps > 0:
         e2e_step()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world) / args.e2e_steps
-    e2e_value = tokens_per_step / (e2e_ms / 1000.0)
+        torch.cuda.synchronize()
+        barrier(world)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.e2e_steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = max_over_ranks(e0.elapsed_time(e1), world) / args.e2e_steps
+        e2e_value = tokens_per_step / (e2e_ms / 1000.0)
 
     nbytes = algorithmic_bytes(c["B"], c["T"], c["H"], c["HK"], c["K"], c["V"], has_h0=inp["initial_state"] is not None)
     peak, peak_kind = load_peaks()
     achieved = nbytes / (per_launch_ms / 1000.0) / 1e9
-    traffic = load_traffic(args.config)
+    plan = cg.ChunkGatedDeltaRuleFwdH(inp["k"], inp["w"], inp["u"], inp["g"], inp["initial_state"], None, None, 64,
+                                      *_plan_outputs(inp, c, dev), layout="token_major", **opts).plan
+    kernel_name = {1: "tc", 2: "general", 3: "tc_fused"}.get(plan["kernel"], str(plan["kernel"]))
+    traffic = load_traffic(args.config, kernel_name)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -422,7 +444,8 @@ def main() -> int:
                 "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
                 "algorithmic_bytes_per_launch": nbytes,
                 "launch_ms": per_launch_ms,
-                "traffic": traffic.get("dram_bytes_per_launch") if traffic else None,
+                "traffic": traffic,
+                "kernel": kernel_name,
             },
             "hbm_gbs_per_gpu": achieved,
             "clocks": clk,
