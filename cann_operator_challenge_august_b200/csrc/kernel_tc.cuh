@@ -62,7 +62,8 @@ struct TcConfig {
     static constexpr int kVoutBytes = 64 * VT * 2;
     static constexpr int kOffS = STAGES * kStageBytes;
     static constexpr int kOffVout = kOffS + kSBytes;
-    static constexpr int kOffBar = kOffVout + kVoutBytes;
+    static constexpr int kOffG = kOffVout + kVoutBytes;  // [STAGES][64] fp32 gate inputs
+    static constexpr int kOffBar = kOffG + STAGES * 64 * 4;
     static constexpr int kNumBars = 2 * STAGES + 5;
     static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;  // + tmem slot, abort flag, alignment
     static constexpr uint32_t kStageTx = kStageBytes;
@@ -79,6 +80,24 @@ __device__ __forceinline__ uint32_t sw128_off(int row, int col, int sub_bytes)
 {
     const int sub = col >> 6, cc = col & 63;
     return sub * sub_bytes + row * 128 + ((((cc >> 3) ^ (row & 7)) & 7) << 4) + ((cc & 7) << 1);
+}
+
+__device__ __forceinline__ void cp_async_4(void* smem_dst, const void* gmem_src)
+{
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src) : "memory");
+}
+
+// Arrive on `bar` once this thread's earlier cp.async copies have landed; the
+// arrival is one of those counted when the barrier was initialised.
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar)
+{
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Pending-group waits of the bulk (TMA) stores issued by this thread.
+__device__ __forceinline__ void bulk_wait_group_read1()
+{
+    asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi)
@@ -133,7 +152,7 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
-            mbar_init(&full[s], 1);
+            mbar_init(&full[s], 1 + 32);  // TMA bytes + 32 cp.async arrivals (gate inputs)
             mbar_init(&empty[s], 1);
         }
         mbar_init(mma1_done, 1);
@@ -168,14 +187,18 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
     if (warp == Cfg::kProducerWarp) {
         // ------------------------------------------------------------ producer
         int64_t issued = 0;
-        if (lane == 0) {
-            for (int64_t c = 0; c < nchunks; ++c) {
-                const int s = static_cast<int>(c % STAGES);
-                const uint32_t use = static_cast<uint32_t>(c / STAGES);
-                if (c >= STAGES && !mbar_wait(&empty[s], (use - 1) & 1, ctl, 0x10)) break;
-                if (p.fault_inject && c == 1) break;  // test hook: consumers' waits must expire
+        const int64_t gbase = si.b * p.g_sb + hv * p.g_sh;
+        for (int64_t c = 0; c < nchunks; ++c) {
+            const int s = static_cast<int>(c % STAGES);
+            const uint32_t use = static_cast<uint32_t>(c / STAGES);
+            bool go = true;
+            if (c >= STAGES && lane == 0) go = mbar_wait(&empty[s], (use - 1) & 1, ctl, 0x10);
+            if (p.fault_inject && c == 1) go = false;  // test hook: consumers' waits must expire
+            go = __shfl_sync(0xffffffffu, go ? 1 : 0, 0) != 0;
+            if (!go) break;
+            const int t0 = static_cast<int>(si.bos + c * kChunk);
+            if (lane == 0) {
                 mbar_arrive_expect_tx(&full[s], Cfg::kStageTx);
-                const int t0 = static_cast<int>(si.bos + c * kChunk);
                 const int b = static_cast<int>(si.b);
 #pragma unroll
                 for (int sub = 0; sub < Cfg::kSubK; ++sub)
@@ -189,10 +212,20 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
                 for (int sub = 0; sub < Cfg::kSubV; ++sub)
                     tma_load_4d(&args.maps.u, smem + s * Cfg::kStageBytes + 2 * Cfg::kTileKBytes + sub * 8192,
                                 &full[s], v0 + sub * 64, static_cast<int>(hv), t0, b);
-                ++issued;
             }
-            // Drain: never leave the CTA while a load may still land in its
-            // shared memory (bounded, and independent of the abort flag).
+            // gate inputs of the chunk: 64 fp32 values at any stride, 2 per lane
+            if (p.g) {
+                const int len = static_cast<int>(si.len - c * kChunk < kChunk ? si.len - c * kChunk : kChunk);
+                float* gs = reinterpret_cast<float*>(smem + Cfg::kOffG) + 64 * s;
+                if (lane < len) cp_async_4(gs + lane, p.g + gbase + (t0 + lane) * p.g_st);
+                if (lane + 32 < len) cp_async_4(gs + lane + 32, p.g + gbase + (t0 + lane + 32) * p.g_st);
+            }
+            cp_async_arrive_noinc(&full[s]);
+            ++issued;
+        }
+        // Drain: never leave the CTA while a load may still land in its
+        // shared memory (bounded, and independent of the abort flag).
+        if (lane == 0) {
             const int64_t first = issued > STAGES ? issued - STAGES : 0;
             WaitCtl drain{never_flag, p.status, p.timeout_ns};
             for (int64_t c = first; c < issued; ++c)
@@ -209,21 +242,22 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
                 if (!mbar_wait(&full[s], static_cast<uint32_t>(c / STAGES) & 1, ctl, 0x20)) break;
                 if (!mbar_wait(s_ready, static_cast<uint32_t>(c) & 1, ctl, 0x20)) break;
                 tc_fence_after();
+                // descriptors differ only in the start-address field (bits 0-13, 16-byte units)
+                const uint64_t a1 = umma_desc_sw128(wc_addr(s), 16, 1024);
+                const uint64_t b1 = umma_desc_sw128(s_addr, Cfg::kSSubBytes, 1024);
 #pragma unroll
-                for (int kk = 0; kk < K_ / 16; ++kk) {
-                    const uint64_t a = umma_desc_sw128(wc_addr(s) + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024);
-                    const uint64_t bdesc = umma_desc_sw128(s_addr + kk * 2048, Cfg::kSSubBytes, 1024);
-                    tc_mma_bf16(d1, a, bdesc, Cfg::kIdesc1, kk > 0 ? 1u : 0u);
-                }
+                for (int kk = 0; kk < K_ / 16; ++kk)
+                    tc_mma_bf16(d1, a1 + static_cast<uint64_t>(((kk >> 2) * 8192 + (kk & 3) * 32) >> 4),
+                                b1 + static_cast<uint64_t>((kk * 2048) >> 4), Cfg::kIdesc1, kk > 0 ? 1u : 0u);
                 tc_commit(mma1_done);
                 if (!mbar_wait(vdec_ready, static_cast<uint32_t>(c) & 1, ctl, 0x20)) break;
                 tc_fence_after();
+                const uint64_t a2 = umma_desc_sw128(kc_addr(s), 8192, 1024);
+                const uint64_t b2 = umma_desc_sw128(uc_addr(s), 8192, 1024);
 #pragma unroll
-                for (int tt = 0; tt < 4; ++tt) {
-                    const uint64_t a = umma_desc_sw128(kc_addr(s) + tt * 2048, 8192, 1024);
-                    const uint64_t bdesc = umma_desc_sw128(uc_addr(s) + tt * 2048, 8192, 1024);
-                    tc_mma_bf16(d2, a, bdesc, Cfg::kIdesc2, tt > 0 ? 1u : 0u);
-                }
+                for (int tt = 0; tt < 4; ++tt)
+                    tc_mma_bf16(d2, a2 + static_cast<uint64_t>((tt * 2048) >> 4), b2 + static_cast<uint64_t>((tt * 2048) >> 4),
+                                Cfg::kIdesc2, tt > 0 ? 1u : 0u);
                 tc_commit(mma2_done);
                 tc_commit(&empty[s]);
             }
@@ -308,6 +342,16 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
             }
         };
 
+        // Swizzled byte offsets of this thread's (row, column pair) elements in
+        // the u / v_decay / v_new tiles: the same for every chunk.
+        constexpr int kPairs = (Cfg::kCW / 32) * 8;  // (column block, 8-column group, row half)
+        uint32_t offs[kPairs];
+#pragma unroll
+        for (int i = 0; i < kPairs; ++i) {
+            const int cb = i >> 3, j = (i >> 1) & 3, half = i & 1;
+            offs[i] = sw128_off(half ? tb : ta, cbase + 32 * cb + 8 * j + pc, 8192);
+        }
+
         bool ok = true;
         write_state_tile();
         fence_proxy_async_smem();
@@ -315,17 +359,6 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
         __syncwarp();
         if (nchunks > 0) store_h(0);
         if (lane == 0) mbar_arrive(s_ready);
-
-        // gate inputs of the current chunk (prefetched one chunk ahead)
-        const int64_t gbase = si.b * p.g_sb + hv * p.g_sh;
-        auto g_at = [&](int64_t t) -> float { return p.g ? __ldg(p.g + gbase + t * p.g_st) : 0.0f; };
-        float g_a = 0.f, g_b = 0.f, g_l = 0.f;
-        if (nchunks > 0) {
-            const int len0 = static_cast<int>(si.len < kChunk ? si.len : kChunk);
-            g_l = g_at(si.bos + len0 - 1);
-            g_a = ta < len0 ? g_at(si.bos + ta) : g_l;
-            g_b = tb < len0 ? g_at(si.bos + tb) : g_l;
-        }
 
         for (int64_t c = 0; c < nchunks && ok; ++c) {
             const int s = static_cast<int>(c % STAGES);
@@ -342,9 +375,13 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
             for (int cb = 0; cb < Cfg::kCW / 32; ++cb)
                 tmem_ld_16x256b_x4(tmem + ((32u * q) << 16) + static_cast<uint32_t>(cbase + 32 * cb), acc[cb]);
             tmem_wait_ld();
-            if (lane == 0) bulk_wait_group_read0();  // v_new staging / S no longer read by old stores
-            __syncwarp();
-
+            const float* gs = reinterpret_cast<const float*>(smem + Cfg::kOffG) + 64 * s;
+            float g_l = 0.f, g_a = 0.f, g_b = 0.f;
+            if (p.g) {
+                g_l = gs[len - 1];
+                g_a = ta < len ? gs[ta] : g_l;
+                g_b = tb < len ? gs[tb] : g_l;
+            }
             float gate_a, gate_b, alpha;
             if (ref) {
                 gate_a = ref_gate(g_l, g_a);
@@ -358,60 +395,61 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
                 gate_a = gate_b = alpha = 1.0f;
             }
             uint8_t* ut = smem + s * Cfg::kStageBytes + 2 * Cfg::kTileKBytes;
+            // Three passes (all loads, all arithmetic, all stores) so that the
+            // shared-memory latencies overlap instead of chaining pair by pair.
+            uint32_t uraw[kPairs], vds[kPairs], vos[kPairs];
 #pragma unroll
-            for (int cb = 0; cb < Cfg::kCW / 32; ++cb) {
+            for (int i = 0; i < kPairs; ++i) uraw[i] = *reinterpret_cast<const uint32_t*>(ut + offs[i]);
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const int col = cbase + 32 * cb + 8 * j + pc;
+            for (int i = 0; i < kPairs; ++i) {
+                const int cb = i >> 3, j = (i >> 1) & 3, half = i & 1;
+                const float gt = half ? gate_b : gate_a;
+                const float a0 = __uint_as_float(acc[cb][4 * j + 2 * half + 0]);
+                const float a1 = __uint_as_float(acc[cb][4 * j + 2 * half + 1]);
+                const float2 uu = unpack_bf16x2(uraw[i]);
+                float vn0, vn1, d0, d1;
+                if (ref) {
+                    vn0 = ref_vnew(uu.x, a0);
+                    vn1 = ref_vnew(uu.y, a1);
+                    d0 = ref_vdecay(vn0, gt);
+                    d1 = ref_vdecay(vn1, gt);
+                } else {
+                    vn0 = uu.x - a0;
+                    vn1 = uu.y - a1;
+                    d0 = vn0 * gt;
+                    d1 = vn1 * gt;
+                }
+                const bool valid = (half ? tb : ta) < len;
+                vos[i] = valid ? pack_bf16x2(vn0, vn1) : 0u;
+                vds[i] = valid ? pack_bf16x2(d0, d1) : 0u;
+            }
+            // v_new staging free: the store of chunk c-1 is read (only h[c]'s may be pending)
+            if (lane == 0) bulk_wait_group_read1();
+            __syncwarp();
 #pragma unroll
-                    for (int half = 0; half < 2; ++half) {
-                        const int t = half ? tb : ta;
-                        const float gt = half ? gate_b : gate_a;
-                        const float a0 = __uint_as_float(acc[cb][4 * j + 2 * half + 0]);
-                        const float a1 = __uint_as_float(acc[cb][4 * j + 2 * half + 1]);
-                        const uint32_t off = sw128_off(t, col, 8192);
-                        uint32_t vd = 0, vo = 0;
-                        if (t < len) {
-                            const float2 uu = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(ut + off));
-                            float vn0, vn1, d0, d1;
-                            if (ref) {
-                                vn0 = ref_vnew(uu.x, a0);
-                                vn1 = ref_vnew(uu.y, a1);
-                                d0 = ref_vdecay(vn0, gt);
-                                d1 = ref_vdecay(vn1, gt);
-                            } else {
-                                vn0 = uu.x - a0;
-                                vn1 = uu.y - a1;
-                                d0 = vn0 * gt;
-                                d1 = vn1 * gt;
-                            }
-                            vo = pack_bf16x2(vn0, vn1);
-                            vd = pack_bf16x2(d0, d1);
-                            if (partial_varlen && p.v_new) {
-                                const int64_t vi = si.b * p.v_sb + (t0 + t) * p.v_st + hv * p.v_sh + v0 + col;
-                                *reinterpret_cast<uint32_t*>(reinterpret_cast<__nv_bfloat16*>(p.v_new) + vi) = vo;
-                            }
-                        }
-                        *reinterpret_cast<uint32_t*>(ut + off) = vd;
-                        *reinterpret_cast<uint32_t*>(vout + off) = vo;
+            for (int i = 0; i < kPairs; ++i) {
+                *reinterpret_cast<uint32_t*>(ut + offs[i]) = vds[i];
+                *reinterpret_cast<uint32_t*>(vout + offs[i]) = vos[i];
+            }
+            if (partial_varlen && p.v_new) {
+#pragma unroll
+                for (int i = 0; i < kPairs; ++i) {
+                    const int cb = i >> 3, j = (i >> 1) & 3, half = i & 1;
+                    const int t = half ? tb : ta;
+                    if (t < len) {
+                        const int64_t vi = si.b * p.v_sb + (t0 + t) * p.v_st + hv * p.v_sh + v0 + cbase + 32 * cb +
+                                           8 * j + pc;
+                        *reinterpret_cast<uint32_t*>(reinterpret_cast<__nv_bfloat16*>(p.v_new) + vi) = vos[i];
                     }
                 }
-            }
-            // prefetch next chunk's gate inputs
-            if (c + 1 < nchunks) {
-                const int64_t tn = t0 + kChunk;
-                const int lenn =
-                    static_cast<int>(si.len - (c + 1) * kChunk < kChunk ? si.len - (c + 1) * kChunk : kChunk);
-                g_l = g_at(tn + lenn - 1);
-                g_a = ta < lenn ? g_at(tn + ta) : g_l;
-                g_b = tb < lenn ? g_at(tn + tb) : g_l;
             }
             fence_proxy_async_smem();
             tc_fence_before();
             __syncwarp();
+            const bool v_stored = p.v_new && !partial_varlen;
             if (lane == 0) {
                 mbar_arrive(vdec_ready);
-                if (p.v_new && !partial_varlen) {
+                if (v_stored) {
 #pragma unroll
                     for (int sub = 0; sub < Cfg::kSubV; ++sub) {
                         if (sub * 64 < cbase || sub * 64 >= cbase + Cfg::kCW) continue;
@@ -426,7 +464,13 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
             if (!mbar_wait(mma2_done, static_cast<uint32_t>(c) & 1, ctl, 0x40)) { ok = false; break; }
             tc_fence_after();
             const bool more = c + 1 < nchunks;
-            if (lane == 0 && more) bulk_wait_group_read0();
+            // S tile free: h[c]'s store is read (chunk c's v_new store may be pending)
+            if (lane == 0 && more) {
+                if (v_stored)
+                    bulk_wait_group_read1();
+                else
+                    bulk_wait_group_read0();
+            }
             __syncwarp();
             if constexpr (K_ == 128) {
 #pragma unroll
