@@ -169,11 +169,13 @@ def barrier(world):
 
 
 def max_over_ranks(x: float, world: int) -> float:
+    """Largest value over all ranks (the device time of the slowest rank)."""
     if world == 1:
         return x
     import torch
     import torch.distributed as dist
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dev = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
 
@@ -215,7 +217,8 @@ def cpu_reference_rate(c, budget_s, n_threads, max_pairs=None):
     sys.path.insert(0, str(ROOT / "tests"))
     from oracle import oracle as o  # the reference arithmetic, restated (timed baseline)
 
-    threads = n_threads or o.max_threads()
+    # every host core this process may run on (torchrun sets OMP_NUM_THREADS=1 for its ranks)
+    threads = n_threads or len(os.sched_getaffinity(0))
     P = max(1, min(threads, max_pairs or threads, c["B"] * c["H"]))
     NT = (c["T"] + 63) // 64
     gen = torch.Generator().manual_seed(0)

@@ -1,6 +1,6 @@
 // Thin inline-PTX wrappers for sm_100a: mbarriers with bounded waits, TMA
 // (cp.async.bulk.tensor) loads/stores, and the tcgen05 tensor-core and
-// tensor-memory instructions.  Nothing here uses cluster multicast.
+// tensor-memory instructions.  Every TMA load here targets this CTA's own shared memory.
 #pragma once
 
 #include <cstdint>
@@ -98,7 +98,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const 
     }
 }
 
-// ---- TMA (no multicast) ----------------------------------------------------------
+// ---- TMA (loads into this CTA only) ----------------------------------------------
 
 __device__ __forceinline__ void tma_load_4d(const CUtensorMap* map, void* smem_dst, uint64_t* bar, int c0, int c1,
                                             int c2, int c3)
