@@ -342,15 +342,10 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
             }
         };
 
-        // Swizzled byte offsets of this thread's (row, column pair) elements in
-        // the u / v_decay / v_new tiles: the same for every chunk.
         constexpr int kPairs = (Cfg::kCW / 32) * 8;  // (column block, 8-column group, row half)
-        uint32_t offs[kPairs];
-#pragma unroll
-        for (int i = 0; i < kPairs; ++i) {
-            const int cb = i >> 3, j = (i >> 1) & 3, half = i & 1;
-            offs[i] = sw128_off(half ? tb : ta, cbase + 32 * cb + 8 * j + pc, 8192);
-        }
+        // Pack v_new after MMA2 is released (64-column tiles); the 10-warp 128-column
+        // configuration packs it with v_decay to stay within its register budget.
+        constexpr bool kDeferVnew = VT == 64;
 
         bool ok = true;
         write_state_tile();
@@ -397,9 +392,18 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
             uint8_t* ut = smem + s * Cfg::kStageBytes + 2 * Cfg::kTileKBytes;
             // Three passes (all loads, all arithmetic, all stores) so that the
             // shared-memory latencies overlap instead of chaining pair by pair.
-            uint32_t uraw[kPairs], vds[kPairs], vos[kPairs];
+            // Swizzled byte offsets of this thread's (row, column pair) elements in
+            // the u / v_decay / v_new tiles.
+            uint32_t offs[kPairs];
+#pragma unroll
+            for (int i = 0; i < kPairs; ++i) {
+                const int cb = i >> 3, j = (i >> 1) & 3, half = i & 1;
+                offs[i] = sw128_off(half ? tb : ta, cbase + 32 * cb + 8 * j + pc, 8192);
+            }
+            uint32_t uraw[kPairs], vds[kPairs], vns[kPairs], vos[kPairs];
 #pragma unroll
             for (int i = 0; i < kPairs; ++i) uraw[i] = *reinterpret_cast<const uint32_t*>(ut + offs[i]);
+            // v_decay only (the MMA2 operand); v_new is packed after MMA2 is released.
 #pragma unroll
             for (int i = 0; i < kPairs; ++i) {
                 const int cb = i >> 3, j = (i >> 1) & 3, half = i & 1;
@@ -407,29 +411,50 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
                 const float a0 = __uint_as_float(acc[cb][4 * j + 2 * half + 0]);
                 const float a1 = __uint_as_float(acc[cb][4 * j + 2 * half + 1]);
                 const float2 uu = unpack_bf16x2(uraw[i]);
-                float vn0, vn1, d0, d1;
+                float d0, d1;
                 if (ref) {
-                    vn0 = ref_vnew(uu.x, a0);
-                    vn1 = ref_vnew(uu.y, a1);
+                    const float vn0 = ref_vnew(uu.x, a0), vn1 = ref_vnew(uu.y, a1);
+                    // v_new is an fp16 value here: keep it exactly as a half pair
+                    __half2 hv = __floats2half2_rn(vn0, vn1);
+                    vns[i] = *reinterpret_cast<uint32_t*>(&hv);
                     d0 = ref_vdecay(vn0, gt);
                     d1 = ref_vdecay(vn1, gt);
                 } else {
-                    vn0 = uu.x - a0;
-                    vn1 = uu.y - a1;
-                    d0 = vn0 * gt;
-                    d1 = vn1 * gt;
+                    d0 = (uu.x - a0) * gt;
+                    d1 = (uu.y - a1) * gt;
                 }
-                const bool valid = (half ? tb : ta) < len;
-                vos[i] = valid ? pack_bf16x2(vn0, vn1) : 0u;
-                vds[i] = valid ? pack_bf16x2(d0, d1) : 0u;
+                vds[i] = (half ? tb : ta) < len ? pack_bf16x2(d0, d1) : 0u;
+                if constexpr (!kDeferVnew) {
+                    const float2 f = ref ? __half22float2(*reinterpret_cast<const __half2*>(&vns[i]))
+                                         : make_float2(uu.x - a0, uu.y - a1);
+                    vos[i] = (half ? tb : ta) < len ? pack_bf16x2(f.x, f.y) : 0u;
+                }
             }
-            // v_new staging free: the store of chunk c-1 is read (only h[c]'s may be pending)
-            if (lane == 0) bulk_wait_group_read1();
-            __syncwarp();
+            // v_decay first: it is all MMA2 waits for.
 #pragma unroll
-            for (int i = 0; i < kPairs; ++i) {
-                *reinterpret_cast<uint32_t*>(ut + offs[i]) = vds[i];
-                *reinterpret_cast<uint32_t*>(vout + offs[i]) = vos[i];
+            for (int i = 0; i < kPairs; ++i) *reinterpret_cast<uint32_t*>(ut + offs[i]) = vds[i];
+            fence_proxy_async_smem();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(vdec_ready);
+            // v_new while MMA2 runs.
+            const bool v_stored = p.v_new && !partial_varlen;
+            if (kDeferVnew && p.v_new) {
+#pragma unroll
+                for (int i = 0; i < kPairs; ++i) {
+                    const int cb = i >> 3, j = (i >> 1) & 3, half = i & 1;
+                    float vn0, vn1;
+                    if (ref) {
+                        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&vns[i]));
+                        vn0 = f.x;
+                        vn1 = f.y;
+                    } else {
+                        const float2 uu = unpack_bf16x2(uraw[i]);
+                        vn0 = uu.x - __uint_as_float(acc[cb][4 * j + 2 * half + 0]);
+                        vn1 = uu.y - __uint_as_float(acc[cb][4 * j + 2 * half + 1]);
+                    }
+                    vos[i] = (half ? tb : ta) < len ? pack_bf16x2(vn0, vn1) : 0u;
+                }
             }
             if (partial_varlen && p.v_new) {
 #pragma unroll
@@ -442,14 +467,15 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
                         *reinterpret_cast<uint32_t*>(reinterpret_cast<__nv_bfloat16*>(p.v_new) + vi) = vos[i];
                     }
                 }
-            }
-            fence_proxy_async_smem();
-            tc_fence_before();
-            __syncwarp();
-            const bool v_stored = p.v_new && !partial_varlen;
-            if (lane == 0) {
-                mbar_arrive(vdec_ready);
-                if (v_stored) {
+            } else if (v_stored) {
+                // staging free: the store of chunk c-1 is read (only h[c]'s may be pending)
+                if (lane == 0) bulk_wait_group_read1();
+                __syncwarp();
+#pragma unroll
+                for (int i = 0; i < kPairs; ++i) *reinterpret_cast<uint32_t*>(vout + offs[i]) = vos[i];
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
 #pragma unroll
                     for (int sub = 0; sub < Cfg::kSubV; ++sub) {
                         if (sub * 64 < cbase || sub * 64 >= cbase + Cfg::kCW) continue;
@@ -464,36 +490,37 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
             if (!mbar_wait(mma2_done, static_cast<uint32_t>(c) & 1, ctl, 0x40)) { ok = false; break; }
             tc_fence_after();
             const bool more = c + 1 < nchunks;
-            // S tile free: h[c]'s store is read (chunk c's v_new store may be pending)
-            if (lane == 0 && more) {
-                if (v_stored)
-                    bulk_wait_group_read1();
-                else
-                    bulk_wait_group_read0();
-            }
-            __syncwarp();
+            // S tile free once h[c]'s store is read (chunk c's v_new store may be pending);
+            // the wait overlaps the TMEM loads.
+            auto wait_s_free = [&]() {
+                if (lane == 0 && more) {
+                    if (v_stored)
+                        bulk_wait_group_read1();
+                    else
+                        bulk_wait_group_read0();
+                }
+                __syncwarp();
+            };
             if constexpr (K_ == 128) {
+                const uint32_t ta2 = tmem + VT + ((32u * q) << 16) + static_cast<uint32_t>(cbase);
 #pragma unroll
                 for (int cb = 0; cb < Cfg::kCW / 32; ++cb) {
-                    uint32_t r0[16], r1[16];
-                    const uint32_t ta2 = tmem + VT + ((32u * q) << 16) + static_cast<uint32_t>(cbase + 32 * cb);
-                    tmem_ld_32x32b_x16(ta2, r0);
-                    tmem_ld_32x32b_x16(ta2 + 16, r1);
+                    uint32_t r[2][16];
+                    tmem_ld_32x32b_x16(ta2 + 32 * cb, r[0]);
+                    tmem_ld_32x32b_x16(ta2 + 32 * cb + 16, r[1]);
+                    if (cb == 0) wait_s_free();
                     tmem_wait_ld();
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        float& s0 = st[32 * cb + i];
-                        float& s1 = st[32 * cb + 16 + i];
-                        if (ref) {
-                            s0 = ref_state(s0, alpha, __uint_as_float(r0[i]));
-                            s1 = ref_state(s1, alpha, __uint_as_float(r1[i]));
-                        } else {
-                            s0 = fmaf(s0, alpha, __uint_as_float(r0[i]));
-                            s1 = fmaf(s1, alpha, __uint_as_float(r1[i]));
+                    for (int j = 0; j < 2; ++j)
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            float& sv = st[32 * cb + 16 * j + i];
+                            sv = ref ? ref_state(sv, alpha, __uint_as_float(r[j][i]))
+                                     : fmaf(sv, alpha, __uint_as_float(r[j][i]));
                         }
-                    }
                 }
             } else {
+                wait_s_free();
 #pragma unroll
                 for (int cb = 0; cb < Cfg::kCW / 32; ++cb) {
                     uint32_t r[16];
@@ -511,8 +538,8 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
                 fence_proxy_async_smem();
                 tc_fence_before();
                 __syncwarp();
+                if (lane == 0) mbar_arrive(s_ready);  // MMA1 and the h store both only read the tile
                 store_h(c + 1);
-                if (lane == 0) mbar_arrive(s_ready);
             } else {
                 tc_fence_before();
             }
