@@ -148,3 +148,86 @@ __device__ __forceinline__ void store_io(void* base, int32_t dt, int64_t i, floa
 }
 
 }  // namespace cgdr
+
+namespace cgdr {
+
+// ---- the reference rounding chain, two elements at a time ---------------------------
+// Packed f16x2 / bf16x2 arithmetic gives the same bits as the scalar chain above
+// for finite operands: an f16 product of two f16 values is exact in fp32, and a
+// single f16 (resp. bf16) rounding of a sum equals fp32-then-f16 (resp. bf16)
+// rounding because fp32 carries at least 2p+2 bits.  Infinite or NaN operands
+// are left to the scalar functions (callers test ref_pair_is_finite first and
+// take the scalar path for the whole warp when any lane is not).
+
+__device__ __forceinline__ uint32_t h2_bits(__half2 x) { return *reinterpret_cast<uint32_t*>(&x); }
+__device__ __forceinline__ __half2 bits_h2(uint32_t x) { return *reinterpret_cast<__half2*>(&x); }
+
+// fp32 pair -> f16 pair, round to nearest, finite overflow saturating to +-65504
+// (cast_to_float16 for finite inputs).
+__device__ __forceinline__ uint32_t f16x2_satfinite(float lo, float hi)
+{
+    uint32_t r;
+    asm("cvt.rn.satfinite.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+
+__device__ __forceinline__ __half2 h2_saturate(__half2 x)
+{
+    return __hmax2(__hmin2(x, __float2half2_rn(65504.0f)), __float2half2_rn(-65504.0f));
+}
+
+// bf16 GEMM output of an fp32 accumulator pair, converted to f16 (the GEMM-to-f16
+// step of the chain, overflow to inf as torch's .to(float16)).
+__device__ __forceinline__ __half2 ref_gemm_to_f16x2(float a0, float a1)
+{
+    const __nv_bfloat162 b = __floats2bfloat162_rn(a0, a1);
+    return __floats2half2_rn(__low2float(b), __high2float(b));
+}
+
+__device__ __forceinline__ uint32_t bf16x2_of_h2(__half2 x)
+{
+    const float2 f = __half22float2(x);
+    const __nv_bfloat162 b = __floats2bfloat162_rn(f.x, f.y);
+    return *reinterpret_cast<const uint32_t*>(&b);
+}
+
+// Epilogue 1 of the reference chain on a pair: v_new (f16 bits) and v_decay (bf16
+// bits) from u (bf16 values), the MMA1 accumulator and the f16 gate.  Requires
+// |u|, |acc| < 65000 and a finite gate.
+__device__ __forceinline__ void ref_vnew_vdecay_x2(float u0, float u1, float a0, float a1, __half2 gate,
+                                                   uint32_t& vn_bits, uint32_t& vd_bits)
+{
+    const __half2 ws = ref_gemm_to_f16x2(a0, a1);
+    const __half2 uh = __floats2half2_rn(u0, u1);
+    const __half2 vn = h2_saturate(__hsub2_rn(uh, ws));
+    const __half2 vd = h2_saturate(__hmul2_rn(vn, gate));
+    vn_bits = h2_bits(vn);
+    vd_bits = bf16x2_of_h2(vd);
+}
+
+// Epilogue 2 of the reference chain on a pair: the new bf16 state from the old
+// one, the f16 alpha and the MMA2 accumulator.  Requires finite state, alpha and
+// accumulator (an infinite update is exact too, but NaN needs the scalar path).
+__device__ __forceinline__ void ref_state_x2(float& s0, float& s1, float a0, float a1, __half2 alpha)
+{
+    const __half2 sh = bits_h2(f16x2_satfinite(s0, s1));
+    const __half2 hd = h2_saturate(__hmul2_rn(sh, alpha));
+    const __half2 up = ref_gemm_to_f16x2(a0, a1);
+    const uint32_t hb = bf16x2_of_h2(hd), ub = bf16x2_of_h2(up);
+    const __nv_bfloat162 sum =
+        __hadd2_rn(*reinterpret_cast<const __nv_bfloat162*>(&hb), *reinterpret_cast<const __nv_bfloat162*>(&ub));
+    s0 = __low2float(sum);
+    s1 = __high2float(sum);
+}
+
+// max that propagates NaN (so a NaN operand fails a later `< bound` test)
+__device__ __forceinline__ float fmax_nan(float a, float b)
+{
+    float r;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+    return r;
+}
+
+__device__ __forceinline__ float max_abs2(float a, float b) { return fmax_nan(fabsf(a), fabsf(b)); }
+
+}  // namespace cgdr

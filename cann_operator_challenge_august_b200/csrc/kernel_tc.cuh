@@ -404,6 +404,37 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
 #pragma unroll
             for (int i = 0; i < kPairs; ++i) uraw[i] = *reinterpret_cast<const uint32_t*>(ut + offs[i]);
             // v_decay only (the MMA2 operand); v_new is packed after MMA2 is released.
+            bool packed_ref = false;
+            if (ref) {
+                // The packed f16x2 chain is exact for finite operands below the f16 range;
+                // any other value in the warp sends the warp through the scalar chain.
+                float m = max_abs2(gate_a, gate_b);
+#pragma unroll
+                for (int i = 0; i < kPairs; ++i) {
+                    const int cb = i >> 3, j = (i >> 1) & 3, half = i & 1;
+                    const float2 uu = unpack_bf16x2(uraw[i]);
+                    m = fmax_nan(m, fmax_nan(max_abs2(uu.x, uu.y),
+                                             max_abs2(__uint_as_float(acc[cb][4 * j + 2 * half]),
+                                                      __uint_as_float(acc[cb][4 * j + 2 * half + 1]))));
+                }
+                packed_ref = __all_sync(0xffffffffu, m < 65000.0f) != 0;
+            }
+            if (packed_ref) {
+                const __half2 ga = __float2half2_rn(gate_a), gb = __float2half2_rn(gate_b);
+#pragma unroll
+                for (int i = 0; i < kPairs; ++i) {
+                    const int cb = i >> 3, j = (i >> 1) & 3, half = i & 1;
+                    const float2 uu = unpack_bf16x2(uraw[i]);
+                    uint32_t vd;
+                    ref_vnew_vdecay_x2(uu.x, uu.y, __uint_as_float(acc[cb][4 * j + 2 * half]),
+                                       __uint_as_float(acc[cb][4 * j + 2 * half + 1]), half ? gb : ga, vns[i], vd);
+                    vds[i] = (half ? tb : ta) < len ? vd : 0u;
+                    if constexpr (!kDeferVnew) {
+                        const float2 f = __half22float2(bits_h2(vns[i]));
+                        vos[i] = (half ? tb : ta) < len ? pack_bf16x2(f.x, f.y) : 0u;
+                    }
+                }
+            } else {
 #pragma unroll
             for (int i = 0; i < kPairs; ++i) {
                 const int cb = i >> 3, j = (i >> 1) & 3, half = i & 1;
@@ -429,6 +460,7 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
                                          : make_float2(uu.x - a0, uu.y - a1);
                     vos[i] = (half ? tb : ta) < len ? pack_bf16x2(f.x, f.y) : 0u;
                 }
+            }
             }
             // v_decay first: it is all MMA2 waits for.
 #pragma unroll
@@ -510,14 +542,35 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
                     tmem_ld_32x32b_x16(ta2 + 32 * cb + 16, r[1]);
                     if (cb == 0) wait_s_free();
                     tmem_wait_ld();
+                    bool packed_ref = false;
+                    if (ref) {
+                        float m = fabsf(alpha);
 #pragma unroll
-                    for (int j = 0; j < 2; ++j)
+                        for (int j = 0; j < 2; ++j)
 #pragma unroll
-                        for (int i = 0; i < 16; ++i) {
-                            float& sv = st[32 * cb + 16 * j + i];
-                            sv = ref ? ref_state(sv, alpha, __uint_as_float(r[j][i]))
-                                     : fmaf(sv, alpha, __uint_as_float(r[j][i]));
-                        }
+                            for (int i = 0; i < 16; i += 2)
+                                m = fmax_nan(m, fmax_nan(max_abs2(st[32 * cb + 16 * j + i], st[32 * cb + 16 * j + i + 1]),
+                                                         max_abs2(__uint_as_float(r[j][i]), __uint_as_float(r[j][i + 1]))));
+                        packed_ref = __all_sync(0xffffffffu, m < INFINITY) != 0;
+                    }
+                    if (packed_ref) {
+                        const __half2 ah = __float2half2_rn(alpha);
+#pragma unroll
+                        for (int j = 0; j < 2; ++j)
+#pragma unroll
+                            for (int i = 0; i < 16; i += 2)
+                                ref_state_x2(st[32 * cb + 16 * j + i], st[32 * cb + 16 * j + i + 1],
+                                             __uint_as_float(r[j][i]), __uint_as_float(r[j][i + 1]), ah);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 2; ++j)
+#pragma unroll
+                            for (int i = 0; i < 16; ++i) {
+                                float& sv = st[32 * cb + 16 * j + i];
+                                sv = ref ? ref_state(sv, alpha, __uint_as_float(r[j][i]))
+                                         : fmaf(sv, alpha, __uint_as_float(r[j][i]));
+                            }
+                    }
                 }
             } else {
                 wait_s_free();
