@@ -50,22 +50,46 @@ CONFIGS = {
     "c3": dict(B=1, T=65536, H=32, HK=32, K=128, V=128, scaling="weak", h0=False),
     # a quarter of the north-star workload (one sequence per head): the small case of ncu captures
     "nsq": dict(B=1, T=8192, H=32, HK=32, K=128, V=128, scaling="weak"),
+    # 16 sequences packed into T=32768 via cu_seqlens (lengths uniform in [64, 4096], multiples of 64)
+    "c4": dict(B=1, T=32768, H=32, HK=32, K=128, V=128, scaling="weak", seqs=16),
 }
 
 
-def algorithmic_bytes(B, T, H, HK, K, V, has_h0=True, store_final=True, save_v=True, final_bytes=4, h0_bytes=4):
-    """Each tensor read or written once: k, w, u, g, v_new, h, h0, final."""
-    NT = (T + 63) // 64
-    N = B
+def varlen_lengths(n_seq, total, seed, lo=64, hi=4096):
+    """Seeded lengths, uniform in [lo, hi], multiples of 64, rescaled to sum to `total`."""
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    lens = np.maximum(64, (rng.integers(lo, hi + 1, size=n_seq) // 64) * 64)
+    lens = np.maximum(64, np.round(lens * (total / lens.sum()) / 64).astype(int) * 64)
+    lens[-1] += total - lens.sum()
+    return [int(x) for x in lens]
+
+
+def algorithmic_bytes(B, T, H, HK, K, V, has_h0=True, store_final=True, save_v=True, final_bytes=4, h0_bytes=4,
+                      N=None, NT=None):
+    """Each tensor read or written once: k, w, u, g, v_new, h, h0, final.
+    N sequences (default B) and NT chunks in h (default B's ceil(T/64))."""
+    NT = (T + 63) // 64 if NT is None else NT
+    N = B if N is None else N
     b = B * T * HK * K * 2 + B * T * H * K * 2 + B * T * H * V * 2 + B * T * H * 4
     if save_v:
         b += B * T * H * V * 2
-    b += B * NT * H * K * V * 2
+    b += (B * NT if N == B else NT) * H * K * V * 2
     if has_h0:
         b += N * H * K * V * h0_bytes
     if store_final:
         b += N * H * K * V * final_bytes
     return b
+
+
+def config_bytes(c, seed, has_h0=True):
+    """Algorithmic bytes of one step of config `c` (its varlen lengths drawn
+    with the same seed as the inputs)."""
+    n_seq, n_chunks = c["B"], None
+    if "seqs" in c:
+        n_seq = c["seqs"]
+        n_chunks = sum((L + 63) // 64 for L in varlen_lengths(c["seqs"], c["T"], seed))
+    return algorithmic_bytes(c["B"], c["T"], c["H"], c["HK"], c["K"], c["V"], has_h0=has_h0, N=n_seq, NT=n_chunks)
 
 
 def load_peaks():
@@ -204,8 +228,18 @@ def gen_inputs(c, seed, device):
     pad = (-T) % 64
     gl = torch.nn.functional.pad(gl, (0, 0, 0, pad)).view(B, (T + pad) // 64, 64, H).cumsum(2).view(B, T + pad, H)
     gl = gl[:, :T].contiguous()
-    h0 = (0.1 * torch.randn(B, H, K, V, device=device, generator=g)) if c.get("h0", True) else None
-    return dict(k=k, w=w, u=u, g=gl, initial_state=h0)
+    N = c.get("seqs", B)
+    h0 = (0.1 * torch.randn(N, H, K, V, device=device, generator=g)) if c.get("h0", True) else None
+    out = dict(k=k, w=w, u=u, g=gl, initial_state=h0)
+    if "seqs" in c:
+        import cann_operator_challenge_august_b200 as cg
+        lens = varlen_lengths(c["seqs"], T, seed)
+        cu = [0]
+        for L in lens:
+            cu.append(cu[-1] + L)
+        out["cu_seqlens"] = torch.tensor(cu, dtype=torch.int64, device=device)
+        out["chunk_indices"] = cg.prepare_chunk_indices(out["cu_seqlens"])
+    return out
 
 
 def cpu_reference_rate(c, budget_s, n_threads, max_pairs=None):
@@ -279,7 +313,7 @@ def run_reference_arm(args, cfg_name, c, world, rank):
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic",
-        "config": config_block(cfg_name, c, world),
+        "config": config_block(cfg_name, c, world, config_bytes(c, 1000 + rank)),
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": desc},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -291,22 +325,30 @@ def _plan_outputs(inp, c, dev):
     """Output tensors shaped for the phase-1 plan query (never launched)."""
     import torch
     B, T, H, K, V = c["B"], c["T"], c["H"], c["K"], c["V"]
-    NT = (T + 63) // 64
+    NT = inp["chunk_indices"].shape[0] if "chunk_indices" in inp else (T + 63) // 64
+    N = c.get("seqs", B)
     return (torch.empty(B, NT, H, K, V, dtype=torch.bfloat16, device=dev),
             torch.empty(B, T, H, V, dtype=torch.bfloat16, device=dev),
-            torch.empty(B, H, K, V, dtype=torch.float32, device=dev))
+            torch.empty(N, H, K, V, dtype=torch.float32, device=dev))
 
 
-def config_block(name, c, world):
-    return {
+def config_block(name, c, world, nbytes):
+    varlen = (f", varlen: {c['seqs']} sequences packed into T (lengths multiples of 64 in [64, 4096])"
+              if "seqs" in c else "")
+    block = {
         "workload": f"{name}: chunk_gated_delta_rule_fwd_h bf16 B={c['B']} T={c['T']} H={c['H']} "
-                    f"K={c['K']} V={c['V']} chunk=64, h0 fp32, final_state fp32, v_new stored"
+                    f"K={c['K']} V={c['V']} chunk=64{varlen}, h0 fp32, final_state fp32, v_new stored"
                     + (" (per rank)" if c["scaling"] == "weak" else f" (heads split over {world} ranks)"),
         "B": c["B"], "T": c["T"], "H": c["H"], "K": c["K"], "V": c["V"], "chunk": 64,
         "tokens_per_step_per_rank": c["B"] * c["T"],
-        "l2": "inputs+outputs ~1.9 GB per rank >> 126 MB L2 (no flush needed)",
-        "parallelism": f"head-sharded x{world}, no collective on the data path",
+        "l2": f"inputs+outputs {nbytes / 1e9:.2f} GB per rank > 126 MB L2 (no flush needed)",
+        "parallelism": (f"{world} independent rank(s), each with the whole workload, no collective"
+                        if c["scaling"] == "weak" else
+                        f"heads split over {world} rank(s), no collective on the data path"),
     }
+    if "seqs" in c:
+        block["sequences"] = c["seqs"]
+    return block
 
 
 def main() -> int:
@@ -343,6 +385,7 @@ def main() -> int:
 
     def step():
         return cg.chunk_gated_delta_rule_fwd_h(inp["k"], inp["w"], inp["u"], inp["g"], inp["initial_state"],
+                                               cu_seqlens=inp.get("cu_seqlens"), chunk_indices=inp.get("chunk_indices"),
                                                **opts)
 
     for _ in range(args.warmup):
@@ -389,7 +432,9 @@ def main() -> int:
 
     def e2e_step():
         d = {n: (x.to(dev, non_blocking=True) if x is not None else None) for n, x in host.items()}
-        o = cg.chunk_gated_delta_rule_fwd_h(d["k"], d["w"], d["u"], d["g"], d["initial_state"], **opts)
+        o = cg.chunk_gated_delta_rule_fwd_h(d["k"], d["w"], d["u"], d["g"], d["initial_state"],
+                                            cu_seqlens=d.get("cu_seqlens"), chunk_indices=d.get("chunk_indices"),
+                                            **opts)
         for dst, src in zip(host_out, o):
             dst.copy_(src, non_blocking=True)
 
@@ -408,10 +453,13 @@ def main() -> int:
         e2e_ms = max_over_ranks(e0.elapsed_time(e1), world) / args.e2e_steps
         e2e_value = tokens_per_step / (e2e_ms / 1000.0)
 
-    nbytes = algorithmic_bytes(c["B"], c["T"], c["H"], c["HK"], c["K"], c["V"], has_h0=inp["initial_state"] is not None)
+    nbytes = config_bytes(c, 1000 + rank, has_h0=inp["initial_state"] is not None)
+    if "chunk_indices" in inp:
+        assert sum((L + 63) // 64 for L in varlen_lengths(c["seqs"], c["T"], 1000 + rank)) == inp["chunk_indices"].shape[0]
     peak, peak_kind = load_peaks()
     achieved = nbytes / (per_launch_ms / 1000.0) / 1e9
-    plan = cg.ChunkGatedDeltaRuleFwdH(inp["k"], inp["w"], inp["u"], inp["g"], inp["initial_state"], None, None, 64,
+    plan = cg.ChunkGatedDeltaRuleFwdH(inp["k"], inp["w"], inp["u"], inp["g"], inp["initial_state"],
+                                      inp.get("cu_seqlens"), inp.get("chunk_indices"), 64,
                                       *_plan_outputs(inp, c, dev), layout="token_major", **opts).plan
     kernel_name = {1: "tc", 2: "general", 3: "tc_fused"}.get(plan["kernel"], str(plan["kernel"]))
     traffic = load_traffic(args.config, kernel_name)
@@ -436,7 +484,7 @@ def main() -> int:
             "dtype": "bf16",
             "data": "synthetic (seeded, generated on device per rank)",
             "numerics": args.numerics,
-            "config": config_block(args.config, c, world),
+            "config": config_block(args.config, c, world, nbytes),
             "gpu_launches": args.steps,
             "roofline": {
                 "bound": "hbm",

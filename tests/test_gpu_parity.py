@@ -314,3 +314,40 @@ def test_bounded_wait_expires_without_fault():
     h, v, f = _run_fla(inp, dev, force_kernel=1)
     oh, ov, of = H.oracle_run(inp, "fp32_state")
     H.assert_close(h, oh, BF_TOL, BF_TOL, "after timeout")
+
+
+def test_varlen_metadata_in_workspace():
+    """The metadata kernel's output (the counterpart of the reference's per-task
+    chunk-offset prefix, op_kernel/chunk_gated_delta_rule_fwd_h.h:308-327):
+    each sequence's first chunk and the longest-first launch order (by token
+    count, ties by index), read back from the workspace after a call."""
+    dev = _cuda()
+    lens = [5, 195, 133, 367, 0, 300, 64]
+    cu = [0]
+    for L in lens:
+        cu.append(cu[-1] + L)
+    inp = H.make_inputs(1, cu[-1], 2, 128, 128, seed=19, cu_seqlens=cu)
+    t = {n: (x.to(dev) if isinstance(x, torch.Tensor) else x) for n, x in inp.items()}
+    ci = cg.prepare_chunk_indices(t["cu_seqlens"])
+    NT = ci.shape[0]
+    N = len(lens)
+    h = torch.empty(1, NT, 2, 128, 128, dtype=torch.bfloat16, device=dev)
+    v = torch.empty_like(t["u"])
+    f = torch.empty(N, 2, 128, 128, dtype=torch.float32, device=dev)
+    op = cg.ChunkGatedDeltaRuleFwdH(t["k"], t["w"], t["u"], t["g"], t["initial_state"], t["cu_seqlens"], ci, 64, h, v,
+                                    f, layout="token_major", numerics="fp32_state")
+    ws = torch.zeros(op.workspace_size, dtype=torch.uint8, device=dev)
+    op(ws)
+    torch.cuda.synchronize()
+    raw = ws.cpu().numpy()
+    base = raw[256:256 + 4 * (N + 1)].view(np.int32)
+    off = 256 + ((4 * (N + 1) + 255) // 256) * 256
+    order = raw[off:off + 4 * N].view(np.int32)
+    chunks = [(L + 63) // 64 for L in lens]
+    assert base.tolist() == list(np.concatenate([[0], np.cumsum(chunks)]))
+    # longest first by token count (which refines the chunk-count order), ties by index
+    assert order.tolist() == sorted(range(N), key=lambda i: (-lens[i], i))
+    assert int(raw[:4].view(np.int32)[0]) == 0  # device status clean
+    oh, ov, of = H.oracle_run(inp, "fp32_state")
+    H.assert_close(h, oh, BF_TOL, BF_TOL, "h")
+    H.assert_close(f, of, BF_TOL, BF_TOL, "final (incl. the empty sequence)")
