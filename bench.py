@@ -362,10 +362,14 @@ def main() -> int:
     ap.add_argument("--v-tile", type=int, default=0)
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--op", choices=["fwd_h", "chunk_o"], default="fwd_h",
+                    help="fwd_h: the recurrence (the headline); chunk_o: the chunk output that consumes it")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     cfg = CONFIGS[args.config]
+    if args.op == "chunk_o" and args.impl == "ours":
+        return main_chunk_o(args)
 
     if args.impl == "reference":
         world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -499,6 +503,158 @@ def main() -> int:
                 "kernel": kernel_name,
             },
             "hbm_gbs_per_gpu": achieved,
+            "clocks": clk,
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": e2e_ms},
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    return 0
+
+
+def chunk_o_bytes(c, n_chunks=None):
+    """Algorithmic bytes of one chunk-output launch: q, k, v_new, g, h read
+    once, o written once."""
+    B, T, H, HK, K, V = c["B"], c["T"], c["H"], c["HK"], c["K"], c["V"]
+    NT = (T + 63) // 64 if n_chunks is None else n_chunks
+    rows = B * NT if n_chunks is None else NT
+    return B * T * (2 * HK * K * 2 + 2 * H * V * 2 + H * 4) + rows * H * K * V * 2
+
+
+def cpu_chunk_o_rate(c, inp, q, h, v_new, budget_s):
+    """The chunk-output oracle (numpy; BLAS threads as numpy configures them)
+    on the first chunks of batch row 0, all heads, scaled to the whole job."""
+    import numpy as np
+    from oracle import gdr_stages as G
+
+    def sample(nc):
+        T = 64 * nc
+        cvt = lambda t: t[:1, :T].float().cpu().numpy()  # noqa: E731
+        return (cvt(q), cvt(inp["k"]), cvt(v_new), h[:1, :nc].float().cpu().numpy(), cvt(inp["g"]))
+
+    def timed(nc):
+        a = sample(nc)
+        t0 = time.perf_counter()
+        G.chunk_o(*a)
+        return time.perf_counter() - t0
+
+    t1 = timed(1)
+    NT = (c["T"] + 63) // 64
+    nc = int(max(1, min(NT, budget_s / max(t1, 1e-4))))
+    dt = timed(nc)
+    job_chunks = c["B"] * NT
+    rate = c["B"] * c["T"] * (nc / dt) / job_chunks
+    threads = int(os.environ.get("OMP_NUM_THREADS", "0") or 0) or len(os.sched_getaffinity(0))
+    desc = (f"{nc} of {job_chunks} (batch row, chunk) tiles, all {c['H']} heads ({dt:.2f} s), scaled linearly "
+            f"to the whole job")
+    return rate, desc, threads
+
+
+def main_chunk_o(args) -> int:
+    """--op chunk_o: the chunk output that consumes fwd_h's h and v_new, on the
+    same workload (h and v_new produced by the recurrence kernel once)."""
+    import torch
+    import cann_operator_challenge_august_b200 as cg
+
+    world, rank, local = dist_setup()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    c = shard(CONFIGS[args.config], world, rank)
+    if "seqs" in c:
+        raise SystemExit("--op chunk_o runs the fixed-length configurations")
+    inp = gen_inputs(c, seed=1000 + rank, device=dev)
+    gen = torch.Generator(device=dev).manual_seed(2000 + rank)
+    q = torch.randn(c["B"], c["T"], c["HK"], c["K"], device=dev, generator=gen)
+    q = (q / q.norm(dim=-1, keepdim=True)).to(torch.bfloat16)
+    h, v_new, _ = cg.chunk_gated_delta_rule_fwd_h(inp["k"], inp["w"], inp["u"], inp["g"], inp["initial_state"])
+    del inp["w"], inp["u"]
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        return cg.chunk_fwd_o(q, inp["k"], v_new, h, inp["g"])
+
+    for _ in range(args.warmup):
+        out = step()
+    torch.cuda.synchronize()
+    uuid = None
+    try:
+        uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:
+        pass
+    clocks = ClockSampler(uuid)
+    clocks.start()
+    time.sleep(0.3)
+    barrier(world)
+    torch.cuda.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * args.steps)]
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_stop = torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for i in range(args.steps):
+        ev[2 * i].record(stream)
+        out = step()
+        ev[2 * i + 1].record(stream)
+    t_stop.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    clk = clocks.stop()
+    elapsed_ms = max_over_ranks(t_start.elapsed_time(t_stop), world)
+    per_launch_ms = max_over_ranks(sum(ev[2 * i].elapsed_time(ev[2 * i + 1]) for i in range(args.steps)) / args.steps,
+                                   world)
+    ms_per_step = elapsed_ms / args.steps
+    tokens_per_step = c["B"] * c["T"] * world
+    value = tokens_per_step / (ms_per_step / 1000.0)
+
+    host = {n: t.cpu().pin_memory() for n, t in (("q", q), ("k", inp["k"]), ("v_new", v_new), ("h", h),
+                                                  ("g", inp["g"]))}
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    host_o = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+    d2h = host_o.numel() * host_o.element_size()
+
+    def e2e_step():
+        d = {n: t.to(dev, non_blocking=True) for n, t in host.items()}
+        host_o.copy_(cg.chunk_fwd_o(d["q"], d["k"], d["v_new"], d["h"], d["g"]), non_blocking=True)
+
+    e2e_ms = e2e_value = None
+    if args.e2e_steps > 0:
+        e2e_step()
+        torch.cuda.synchronize()
+        barrier(world)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.e2e_steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = max_over_ranks(e0.elapsed_time(e1), world) / args.e2e_steps
+        e2e_value = tokens_per_step / (e2e_ms / 1000.0)
+
+    nbytes = chunk_o_bytes(c)
+    peak, peak_kind = load_peaks()
+    achieved = nbytes / (per_launch_ms / 1000.0) / 1e9
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rate, desc, threads = cpu_chunk_o_rate(c, inp, q, h, v_new, 10.0)
+        cpu = {"value": rate, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": desc}
+    if rank == 0:
+        line = {
+            "metric": "chunk_o tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+            "scaling": c["scaling"], "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded, generated on device per rank; h and v_new from the recurrence kernel)",
+            "config": dict(config_block(args.config, c, world, nbytes),
+                           workload=f"{args.config}: chunk output bf16 B={c['B']} T={c['T']} H={c['H']} "
+                                    f"K={c['K']} V={c['V']} chunk=64 (q, k, v_new, h, g in; o out)"),
+            "gpu_launches": args.steps,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                         else "fallback",
+                         "algorithmic_bytes_per_launch": nbytes, "launch_ms": per_launch_ms,
+                         "traffic": load_traffic(args.config, "chunk_o"), "kernel": "chunk_o"},
             "clocks": clk,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": e2e_ms},

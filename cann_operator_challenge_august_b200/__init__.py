@@ -1,8 +1,9 @@
 """B200-native (sm_100a) ChunkGatedDeltaRuleFwdH -- the chunked gated-delta-rule
 forward hidden-state recurrence of Gated DeltaNet prefill.
 
-The compute is a CUDA library with a C ABI (include/cgdr_fwd_h.h); this
-package is its Python host side.  See :mod:`.api` for the entry points.
+The compute is a CUDA library with a C ABI (include/cgdr_fwd_h.h for the
+recurrence, include/cgdr_chunk_o.h for the chunk output that consumes it);
+this package is its Python host side.  See :mod:`.api` and :mod:`.gdr`.
 """
 
 from .api import (  # noqa: F401
@@ -14,6 +15,7 @@ from .api import (  # noqa: F401
     read_device_status,
     run,
 )
+from .gdr import ChunkGatedDeltaRuleFwdO, chunk_fwd_o  # noqa: F401
 from ._lib import CgdrError, CgdrValueError  # noqa: F401
 
 __all__ = [
@@ -24,6 +26,8 @@ __all__ = [
     "prepare_chunk_offsets",
     "read_device_status",
     "run",
+    "ChunkGatedDeltaRuleFwdO",
+    "chunk_fwd_o",
     "CgdrError",
     "CgdrValueError",
 ]

@@ -1,4 +1,4 @@
-"""ctypes binding of the C ABI in include/cgdr_fwd_h.h.
+"""ctypes binding of the C ABI in include/*.h.
 
 The shared library is built in-tree (``python -m
 cann_operator_challenge_august_b200.build``).  There is no fallback: if the
@@ -33,18 +33,27 @@ NOALLOC_SCRATCH_BYTES = 65536  # CGDR_NOALLOC_SCRATCH_BYTES
 DEVICE_WAIT_TIMEOUT = 0x1
 DEVICE_BAD_VARLEN = 0x2
 
-# Every symbol declared in include/cgdr_fwd_h.h.
-EXPORTS = (
-    "cgdrChunkGatedDeltaRuleFwdHGetWorkspaceSize",
-    "cgdrChunkGatedDeltaRuleFwdHGetWorkspaceSizeEx",
-    "cgdrChunkGatedDeltaRuleFwdH",
-    "cgdrChunkGatedDeltaRuleFwdHNoAlloc",
-    "cgdrDestroyExecutor",
-    "cgdrGetPlan",
-    "cgdrReadDeviceStatus",
-    "cgdrGetLastErrorMessage",
-    "cgdrGetAbiVersion",
-)
+# Every symbol declared in include/*.h, by header.
+EXPORTS_BY_HEADER = {
+    "cgdr_fwd_h.h": (
+        "cgdrChunkGatedDeltaRuleFwdHGetWorkspaceSize",
+        "cgdrChunkGatedDeltaRuleFwdHGetWorkspaceSizeEx",
+        "cgdrChunkGatedDeltaRuleFwdH",
+        "cgdrChunkGatedDeltaRuleFwdHNoAlloc",
+        "cgdrDestroyExecutor",
+        "cgdrGetPlan",
+        "cgdrReadDeviceStatus",
+        "cgdrGetLastErrorMessage",
+        "cgdrGetAbiVersion",
+    ),
+    "cgdr_chunk_o.h": (
+        "cgdrChunkGatedDeltaRuleFwdOGetWorkspaceSize",
+        "cgdrChunkGatedDeltaRuleFwdO",
+        "cgdrDestroyChunkOExecutor",
+        "cgdrChunkOGridSize",
+    ),
+}
+EXPORTS = tuple(sym for syms in EXPORTS_BY_HEADER.values() for sym in syms)
 
 
 class CgdrTensor(ctypes.Structure):
@@ -68,6 +77,10 @@ class CgdrFwdHOptions(ctypes.Structure):
         ("fault_inject", ctypes.c_int32),
         ("reserved", ctypes.c_int32),
     ]
+
+
+class CgdrChunkOOptions(ctypes.Structure):
+    _fields_ = [("wait_timeout_ms", ctypes.c_int32), ("reserved", ctypes.c_int32 * 7)]
 
 
 class CgdrFwdHPlan(ctypes.Structure):
@@ -118,6 +131,15 @@ def load() -> ctypes.CDLL:
     lib.cgdrReadDeviceStatus.restype = ctypes.c_int
     lib.cgdrGetLastErrorMessage.argtypes = []
     lib.cgdrGetLastErrorMessage.restype = ctypes.c_char_p
+    lib.cgdrChunkGatedDeltaRuleFwdOGetWorkspaceSize.argtypes = (
+        [T] * 7 + [ctypes.c_double, ctypes.c_int64, T, ctypes.POINTER(CgdrChunkOOptions), u64p, exp])
+    lib.cgdrChunkGatedDeltaRuleFwdOGetWorkspaceSize.restype = ctypes.c_int
+    lib.cgdrChunkGatedDeltaRuleFwdO.argtypes = [ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p, ctypes.c_void_p]
+    lib.cgdrChunkGatedDeltaRuleFwdO.restype = ctypes.c_int
+    lib.cgdrDestroyChunkOExecutor.argtypes = [ctypes.c_void_p]
+    lib.cgdrDestroyChunkOExecutor.restype = None
+    lib.cgdrChunkOGridSize.argtypes = [ctypes.c_void_p]
+    lib.cgdrChunkOGridSize.restype = ctypes.c_int64
     lib.cgdrGetAbiVersion.argtypes = []
     lib.cgdrGetAbiVersion.restype = ctypes.c_int32
     _lib = lib

@@ -18,8 +18,8 @@ from pathlib import Path
 PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 LIB = PKG / "libcgdr_fwd_h.so"
-SOURCES = [PKG / "csrc" / "cgdr_fwd_h.cu"]
-HEADERS = sorted((PKG / "csrc").glob("*.cuh")) + [ROOT / "include" / "cgdr_fwd_h.h"]
+SOURCES = [PKG / "csrc" / n for n in ("cgdr_fwd_h.cu", "cgdr_chunk_o.cu", "host_util.cu")]
+HEADERS = sorted((PKG / "csrc").glob("*.cuh")) + sorted((ROOT / "include").glob("*.h"))
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -7,30 +7,19 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
-#include <cstdarg>
-#include <cstdio>
 #include <cstring>
 #include <new>
 
 #include "../../include/cgdr_fwd_h.h"
 #include "common.cuh"
+#include "host_util.cuh"
 #include "kernel_simt.cuh"
 #include "kernel_tc.cuh"
 
 using namespace cgdr;
+using namespace cgdr::host;
 
 namespace {
-
-thread_local char g_err[512] = "";
-
-cgdrStatus fail(cgdrStatus st, const char* fmt, ...)
-{
-    va_list ap;
-    va_start(ap, fmt);
-    vsnprintf(g_err, sizeof(g_err), fmt, ap);
-    va_end(ap);
-    return st;
-}
 
 constexpr int64_t kMaxTokens = 256 * 1024;  // infershape.cpp:32
 constexpr int64_t kMaxValueHeads = 128;     // infershape.cpp:33
@@ -39,10 +28,6 @@ constexpr int64_t kMinHeadDim = 32;         // infershape.cpp:35
 constexpr int64_t kMaxHeadDim = 256;        // infershape.cpp:36
 constexpr int64_t kMaxSequences = 4;        // infershape.cpp:31
 constexpr uint64_t kHeaderBytes = 256;      // workspace: device status word
-
-uint64_t align256(uint64_t x) { return (x + 255) & ~uint64_t(255); }
-
-bool present(const cgdrTensor* t) { return t != nullptr && t->data != nullptr; }
 
 }  // namespace
 
@@ -63,31 +48,6 @@ constexpr uint32_t kMagic = 0xC6D2F0A1u;
 struct Dims {
     int64_t B, T, HK, HV, K, V, N, NT;
 };
-
-cgdrStatus check_rank(const cgdrTensor* t, int rank, const char* name)
-{
-    if (t->ndim != rank) return fail(CGDR_STATUS_BAD_RANK, "%s must have rank %d, got %d", name, rank, t->ndim);
-    return CGDR_STATUS_SUCCESS;
-}
-
-cgdrStatus check_inner_contiguous(const cgdrTensor* t, const char* name)
-{
-    if (t->shape[t->ndim - 1] > 1 && t->strides[t->ndim - 1] != 1)
-        return fail(CGDR_STATUS_BAD_STRIDE, "%s must be contiguous in its last dimension", name);
-    for (int i = 0; i < t->ndim; ++i)
-        if (t->shape[i] < 0 || t->strides[i] < 0)
-            return fail(CGDR_STATUS_BAD_STRIDE, "%s has a negative extent or stride", name);
-    return CGDR_STATUS_SUCCESS;
-}
-
-bool shape_is(const cgdrTensor* t, std::initializer_list<int64_t> s)
-{
-    if (t->ndim != static_cast<int>(s.size())) return false;
-    int i = 0;
-    for (int64_t x : s)
-        if (t->shape[i++] != x) return false;
-    return true;
-}
 
 int io_of(int32_t dt) { return dt == CGDR_DT_BF16 ? kBF16 : (dt == CGDR_DT_FLOAT32 ? kF32 : 0); }
 
@@ -357,45 +317,6 @@ cgdrStatus build(const cgdrTensor* k, const cgdrTensor* w, const cgdrTensor* u, 
 }
 
 // ---- tensor maps ----------------------------------------------------------------
-
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn()
-{
-    static EncodeTiledFn fn = nullptr;
-    if (!fn) {
-        void* ptr = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeTiledFn>(ptr);
-    }
-    return fn;
-}
-
-// A bf16 tensor map with 128-byte swizzle over `rank` dims given innermost
-// first (sizes in elements, strides in elements for dims 1..rank-1).
-cgdrStatus make_map(CUtensorMap* map, void* base, int rank, const int64_t* size, const int64_t* stride,
-                    const uint32_t* box, const char* name)
-{
-    EncodeTiledFn fn = encode_fn();
-    if (!fn) return fail(CGDR_STATUS_CUDA_ERROR, "cuTensorMapEncodeTiled is unavailable");
-    cuuint64_t gdim[5], gstride[4];
-    cuuint32_t bdim[5], estride[5];
-    for (int i = 0; i < rank; ++i) {
-        gdim[i] = static_cast<cuuint64_t>(size[i] > 0 ? size[i] : 1);
-        bdim[i] = box[i];
-        estride[i] = 1;
-    }
-    for (int i = 1; i < rank; ++i) gstride[i - 1] = static_cast<cuuint64_t>(stride[i]) * 2;
-    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, base, gdim, gstride, bdim, estride,
-                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return fail(CGDR_STATUS_CUDA_ERROR, "cuTensorMapEncodeTiled(%s) failed: %d", name, (int)r);
-    return CGDR_STATUS_SUCCESS;
-}
 
 cgdrStatus build_maps(const cgdrExecutor* ex, TcMaps* m)
 {

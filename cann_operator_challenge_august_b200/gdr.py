@@ -1,0 +1,101 @@
+"""Python front ends of the stages around the hidden-state recurrence, over
+the C ABI in include/cgdr_chunk_o.h.
+
+* :class:`ChunkGatedDeltaRuleFwdO` -- two-phase call of the chunk output
+  (workspace query, then launch into a caller-owned ``o``).
+* :func:`chunk_fwd_o` -- allocate-and-call form with the argument set of the
+  fla ``chunk_fwd_o`` wrapper.
+
+The chunk output is the consumer of ``chunk_gated_delta_rule_fwd_h``'s ``h``
+and ``v_new``: per 64-token chunk, ``o = q' h[c] + P v_new`` with
+``q' = bf16(q * scale * exp(g))`` and ``P = bf16(bf16(q k^T) * scale *
+exp(g_i - g_j))`` on and below the diagonal (the reference's stage 2
+inter-chunk term and stage 3, ref/chunk_gated_delta_rule/tests/pytest/
+chunk_gated_delta_rule_benchmark.py:77-79, :129, :145-175).
+
+Nothing here computes on the CPU: the CUDA library does the work and raises
+if it is missing.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+from .api import CHUNK_SIZE, _desc, _require_cuda, _stream_handle, prepare_chunk_indices, read_device_status
+
+
+class ChunkGatedDeltaRuleFwdO:
+    """Two-phase chunk output: ``op = ChunkGatedDeltaRuleFwdO(q, k, v_new, h,
+    g, cu_seqlens, chunk_indices, scale, chunk_size, o)`` validates and plans;
+    ``op(workspace)`` enqueues the kernel on the current stream.  Launched at
+    most once."""
+
+    def __init__(self, q, k, v_new, h, g, cu_seqlens, chunk_indices, scale, chunk_size, o, *, wait_timeout_ms=0):
+        lib = _lib.load()
+        self._keep = (q, k, v_new, h, g, cu_seqlens, chunk_indices, o)
+        ws = ctypes.c_uint64(0)
+        ex = ctypes.c_void_p(None)
+        opt = _lib.CgdrChunkOOptions(wait_timeout_ms=int(wait_timeout_ms))
+        descs = [_desc(x) for x in (q, k, v_new, h, g, cu_seqlens, chunk_indices)]
+        st = lib.cgdrChunkGatedDeltaRuleFwdOGetWorkspaceSize(
+            *[ctypes.byref(d) for d in descs], float(scale if scale is not None else 0.0), int(chunk_size),
+            ctypes.byref(_desc(o)), ctypes.byref(opt), ctypes.byref(ws), ctypes.byref(ex))
+        _lib.check(st, "cgdrChunkGatedDeltaRuleFwdOGetWorkspaceSize")
+        self._ex = ex
+        self.workspace_size = int(ws.value)
+
+    @property
+    def grid(self) -> int:
+        if self._ex is None:
+            raise RuntimeError("executor already consumed")
+        return int(_lib.load().cgdrChunkOGridSize(self._ex))
+
+    def __call__(self, workspace: torch.Tensor, stream: int | None = None) -> None:
+        if self._ex is None:
+            raise RuntimeError("executor already consumed")
+        ex, self._ex = self._ex, None
+        if stream is None:
+            stream = _stream_handle(workspace.device)
+        st = _lib.load().cgdrChunkGatedDeltaRuleFwdO(
+            ctypes.c_void_p(workspace.data_ptr()), workspace.numel() * workspace.element_size(), ex,
+            ctypes.c_void_p(stream))
+        _lib.check(st, "cgdrChunkGatedDeltaRuleFwdO")
+
+    def __del__(self):
+        if getattr(self, "_ex", None) is not None and _lib._lib is not None:
+            _lib._lib.cgdrDestroyChunkOExecutor(self._ex)
+            self._ex = None
+
+
+def chunk_fwd_o(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v_new: torch.Tensor,
+    h: torch.Tensor,
+    g: torch.Tensor | None = None,
+    scale: float | None = None,
+    cu_seqlens: torch.LongTensor | None = None,
+    chunk_size: int = CHUNK_SIZE,
+    chunk_indices: torch.Tensor | None = None,
+    *,
+    check_device_status: bool = False,
+) -> torch.Tensor:
+    """Chunk output ``o [B,T,H,V]`` (bf16) from q, k ``[B,T,Hg,K]``, v_new
+    ``[B,T,H,V]``, h ``[B,NT,H,K,V]`` and the chunk-local cumulative gate g
+    ``[B,T,H]``.  ``scale`` defaults to ``K ** -0.5``.  With cu_seqlens and no
+    chunk_indices the chunk list is derived on the host (one sync)."""
+    _require_cuda(q, k, v_new, h, g, cu_seqlens, chunk_indices)
+    if cu_seqlens is not None and chunk_indices is None:
+        chunk_indices = prepare_chunk_indices(cu_seqlens, chunk_size)
+    o = torch.empty_like(v_new)
+    op = ChunkGatedDeltaRuleFwdO(q, k, v_new, h, g, cu_seqlens, chunk_indices, scale, chunk_size, o)
+    ws = torch.empty(max(op.workspace_size, 256), dtype=torch.uint8, device=q.device)
+    op(ws)
+    if check_device_status:
+        status = read_device_status(ws)
+        if status:
+            raise RuntimeError(f"device status 0x{status:x}")
+    return o

@@ -1,0 +1,348 @@
+"""numpy restatement of the reference's chunked Gated DeltaNet stages --
+TEST INFRASTRUCTURE ONLY.
+
+Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU legs may
+import this module.  It is the checker; the product never routes through it.
+
+It restates, in float32 numpy with explicit bf16 rounding, the reference's
+bf16 operator (ref/chunk_gated_delta_rule/tests/pytest/
+chunk_gated_delta_rule_benchmark.py) and its fp32 golden
+(ref/chunk_gated_delta_rule/tests/pytest/chunk_gated_delta_rule_golden.py),
+plus the reference's three-party accuracy check
+(ref/chunk_gated_delta_rule/tests/assets/impl/compare.py).  Line numbers in
+the docstrings refer to those files.
+
+Rounding model: a torch bf16 @ bf16 product accumulates in float32 and rounds
+once to bf16; a bf16 + bf16 sum is computed in float32 and rounded once; a
+float32 cumsum on the CPU accumulates in float64 (torch's CPU accumulate
+type) and rounds once.  numpy float32 matmul sums in another order, so the
+restatement matches the reference to within float32 summation order.
+
+Layouts follow the reference API (TND): q, k ``[T, Nk, Dk]``, v ``[T, Nv,
+Dv]``, beta, g ``[T, Nv]``, state ``[B, Nv, Dv, Dk]``.  The fla-layout
+helpers (``chunk_o``) take ``[B, T, H, *]`` arrays.  bf16 arrays are float32
+numpy arrays holding bf16 values.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+try:  # scipy's triangular solve (LAPACK trsm), the same routine family torch uses
+    from scipy.linalg import solve_triangular as _solve_tri
+except ImportError:  # pragma: no cover
+    _solve_tri = None
+
+from .oracle import bf16_bits_to_f32, f32_to_bf16_bits
+
+C = 64
+
+
+def bf16r(x) -> np.ndarray:
+    """Round float32 values to bf16 (round to nearest even), kept as float32."""
+    return bf16_bits_to_f32(f32_to_bf16_bits(np.asarray(x, dtype=np.float32)))
+
+
+def _mm(a, b) -> np.ndarray:
+    return np.matmul(a.astype(np.float32), b.astype(np.float32))
+
+
+def _cumsum_f32(x, axis=-1) -> np.ndarray:
+    return np.cumsum(x.astype(np.float64), axis=axis).astype(np.float32)
+
+
+def _exp(x) -> np.ndarray:
+    return np.exp(x.astype(np.float32)).astype(np.float32)
+
+
+# ---- stage 1: WY representation (benchmark.py:14-93) --------------------------------
+
+def stage1(q, k, v, g, beta, scale):
+    """One sequence, all heads: q, k ``[S, Nv, Dk]`` (already repeated to the
+    value heads), v ``[S, Nv, Dv]``, g, beta ``[S, Nv]``.  Returns a dict of
+    ``[Nv, Sp, *]`` arrays (Sp = S padded to a multiple of 64): g_cum,
+    k_cumdecay, v_inner, q_prime, kg, qkt (benchmark.py:86-93)."""
+    S, Nv, Dk = q.shape
+    Dv = v.shape[2]
+    Sp = (S + C - 1) // C * C
+    nc = Sp // C
+
+    def pad(t):
+        out = np.zeros((Sp,) + t.shape[1:], dtype=np.float32)
+        out[:S] = t
+        return out
+
+    def chunks(t):  # [Sp, Nv, D] -> [Nv*nc, C, D] ; [Sp, Nv] -> [Nv*nc, C]
+        t = pad(t)
+        if t.ndim == 3:
+            return np.ascontiguousarray(t.transpose(1, 0, 2)).reshape(Nv * nc, C, t.shape[2])
+        return np.ascontiguousarray(t.transpose(1, 0)).reshape(Nv * nc, C)
+
+    qa, ka, va, ga, ba = chunks(q), chunks(k), chunks(v), chunks(g), chunks(beta)
+    bf = ba[..., None]
+    kkt = bf16r(_mm(ka, ka.transpose(0, 2, 1))) * bf                          # :59
+    qkt = bf16r(_mm(qa, ka.transpose(0, 2, 1)))                               # :60
+    g_cum = _cumsum_f32(ga, -1)                                               # :62
+    g_cum_exp = _exp(g_cum)                                                   # :63
+    lower = np.tril(np.ones((C, C), dtype=bool), -1)                          # :65
+    diff = g_cum[:, :, None] - g_cum[:, None, :]                              # :66
+    attn = _exp(diff * lower) * lower                                         # :67
+    A = np.eye(C, dtype=np.float32) + kkt * attn                              # :69-70
+    attn_1 = np.empty_like(A)
+    eye = np.eye(C, dtype=np.float32)
+    for i in range(A.shape[0]):
+        if _solve_tri is not None:
+            attn_1[i] = _solve_tri(A[i], eye, lower=True, check_finite=False)
+        else:  # pragma: no cover
+            attn_1[i] = np.linalg.solve(A[i], eye)
+    attn_1 = bf16r(attn_1)                                                    # :71
+    kg = ka * _exp(g_cum[:, -1, None] - g_cum)[..., None]                     # :73
+    k_cumdecay = ((bf * g_cum_exp[:, :, None]) * np.float32(-1)) * ka        # :74
+    v_beta = bf16r(va * bf)                                                   # :76
+    q_prime = bf16r((qa * np.float32(scale)) * g_cum_exp[:, :, None])        # :77-79
+    v_inner = bf16r(_mm(attn_1, v_beta))                                      # :81
+    k_cumdecay = bf16r(_mm(attn_1, bf16r(k_cumdecay)))                        # :82
+    kg = bf16r(kg)                                                            # :83
+    return dict(
+        g_cum=g_cum.reshape(Nv, Sp), k_cumdecay=k_cumdecay.reshape(Nv, Sp, Dk),
+        v_inner=v_inner.reshape(Nv, Sp, Dv), q_prime=q_prime.reshape(Nv, Sp, Dk),
+        kg=kg.reshape(Nv, Sp, Dk), qkt=qkt.reshape(Nv, Sp, C))
+
+
+# ---- stage 2: recurrence (benchmark.py:96-142) ---------------------------------------
+
+def stage2(q_prime, v_inner, g_cum, k_cumdecay, state, kg):
+    """Returns (final_state bf16 ``[Nv, Dv, Dk]``, attn_inter ``[Nv, Sp, Dv]``,
+    v_new ``[Nv, Sp, Dv]``, states ``[nc, Nv, Dv, Dk]`` -- the state before each
+    chunk)."""
+    Nv, Sp, Dv = v_inner.shape
+    nc = Sp // C
+    attn_inter = np.zeros((Nv, Sp, Dv), dtype=np.float32)
+    v_new = np.zeros((Nv, Sp, Dv), dtype=np.float32)
+    states = np.zeros((nc,) + state.shape, dtype=np.float32)
+    cur = state.astype(np.float32)                                            # :114
+    for i in range(nc):
+        s, e = i * C, (i + 1) * C
+        states[i] = cur
+        sT = cur.transpose(0, 2, 1)                                           # :127
+        attn_inter[:, s:e] = bf16r(_mm(q_prime[:, s:e], sT))                  # :129
+        v_prime = bf16r(_mm(k_cumdecay[:, s:e], sT))                          # :130
+        vn = bf16r(v_inner[:, s:e] + v_prime)                                 # :131
+        out = bf16r(_mm(vn.transpose(0, 2, 1), kg[:, s:e]))                   # :133
+        decay = _exp(g_cum[:, s:e])[:, -1][:, None, None]                     # :134
+        old = bf16r(cur * decay)                                              # :135
+        cur = bf16r(old + out)                                                # :136
+        v_new[:, s:e] = vn
+    return bf16r(cur), attn_inter, v_new, states
+
+
+# ---- stage 3: chunk output (benchmark.py:145-175) ------------------------------------
+
+def stage3(qkt, scale, g_cum, attn_inter, v_new):
+    Nv, Sp, Dv = attn_inter.shape
+    nc = Sp // C
+    qa = qkt.reshape(Nv * nc, C, C)
+    ga = g_cum.reshape(Nv * nc, C)
+    ai = attn_inter.reshape(Nv * nc, C, Dv)
+    vn = v_new.reshape(Nv * nc, C, Dv)
+    lower = np.tril(np.ones((C, C), dtype=bool), 0)                           # :163
+    diff = ga[:, :, None] - ga[:, None, :]                                    # :164
+    decay = _exp(diff * lower) * lower                                        # :167
+    masked = (qa * np.float32(scale)) * decay                                 # :168
+    inner = bf16r(_mm(bf16r(masked), vn))                                     # :169
+    out = bf16r(ai + inner)                                                   # :170
+    return out.reshape(Nv, Sp, Dv).transpose(1, 0, 2)                         # :173
+
+
+def benchmark_op(q, k, v, beta, scale, initial_state, seq_lens, g=None):
+    """chunk_gdn_benchmark_opt (benchmark.py:178-224): the reference's bf16
+    operator.  Returns (out ``[T, Nv, Dv]``, final_state ``[B, Nv, Dv, Dk]``)
+    plus the per-sequence stage outputs for inspection."""
+    T, Nk, Dk = q.shape
+    B, Nv, Dv, _ = initial_state.shape
+    if g is None:
+        g = np.zeros((T, Nv), dtype=np.float32)
+    rep = Nv // Nk
+    out = np.zeros((T, Nv, Dv), dtype=np.float32)
+    final = np.zeros((B, Nv, Dv, Dk), dtype=np.float32)
+    stages = []
+    start = 0
+    for b in range(B):
+        S = int(seq_lens[b])
+        end = start + S
+        qs, ks = q[start:end], k[start:end]
+        if rep > 1:
+            qs, ks = np.repeat(qs, rep, axis=1), np.repeat(ks, rep, axis=1)
+        s1 = stage1(qs, ks, v[start:end], g[start:end], beta[start:end], scale)
+        fin, ai, vn, states = stage2(s1["q_prime"], s1["v_inner"], s1["g_cum"], s1["k_cumdecay"],
+                                     initial_state[b], s1["kg"])
+        final[b] = fin
+        out[start:end] = stage3(s1["qkt"], scale, s1["g_cum"], ai, vn)[:S]
+        stages.append(dict(s1, attn_inter=ai, v_new=vn, states=states))
+        start = end
+    return out, final, stages
+
+
+# ---- fp32 golden (chunk_gated_delta_rule_golden.py:73-157) ---------------------------
+
+def golden_op(q, k, v, beta, initial_state, seq_lens, g=None, state_bf16=True):
+    """The reference's fp32 golden, through its adapter
+    (tests/assets/impl/golden.py:106-150): scale = Dk ** -0.5 whatever the
+    caller's scale (chunk_gated_delta_rule_golden.py:98), states transposed
+    to ``[Dk, Dv]`` inside, out cast to the query dtype (bf16) and the final
+    state to the initial state's dtype (golden.py:148-149).  Returns (out
+    ``[T, Nv, Dv]``, final_state ``[B, Nv, Dv, Dk]``)."""
+    T, Nk, Dk = q.shape
+    B, Nv, Dv, _ = initial_state.shape
+    rep = Nv // Nk
+    if g is None:
+        g = np.zeros((T, Nv), dtype=np.float32)
+    out = np.zeros((T, Nv, Dv), dtype=np.float32)
+    final = np.zeros((B, Nv, Dv, Dk), dtype=np.float32)
+    start = 0
+    for b in range(B):
+        S = int(seq_lens[b])
+        end = start + S
+        qs, ks = q[start:end].astype(np.float32), k[start:end].astype(np.float32)
+        if rep > 1:
+            qs, ks = np.repeat(qs, rep, axis=1), np.repeat(ks, rep, axis=1)
+        o, st = _golden_seq(qs, ks, v[start:end], g[start:end], beta[start:end],
+                            initial_state[b].transpose(0, 2, 1).astype(np.float32))
+        out[start:end] = o
+        final[b] = st.transpose(0, 2, 1)
+        start = end
+    return bf16r(out), (bf16r(final) if state_bf16 else final)
+
+
+def _golden_seq(q, k, v, g, beta, state):
+    """One sequence of chunk_gated_delta_rule_native (golden.py:73-157);
+    q, k ``[S, Nv, Dk]``, v ``[S, Nv, Dv]``, state ``[Nv, Dk, Dv]``."""
+    S, Nv, Dk = q.shape
+    pad = (C - S % C) % C
+    tr = lambda t: np.ascontiguousarray(np.swapaxes(t, 0, 1)).astype(np.float32)  # noqa: E731
+    q, k, v, beta, g = tr(q), tr(k), tr(v), tr(beta), tr(g)
+    q = np.pad(q, ((0, 0), (0, pad), (0, 0)))
+    k = np.pad(k, ((0, 0), (0, pad), (0, 0)))
+    v = np.pad(v, ((0, 0), (0, pad), (0, 0)))
+    beta = np.pad(beta, ((0, 0), (0, pad)))
+    g = np.pad(g, ((0, 0), (0, pad)))
+    Sp = S + pad
+    nc = Sp // C
+    scale = np.float32(1.0 / Dk ** 0.5)                                       # :98
+    q = q * scale                                                             # :99
+    v_beta = v * beta[..., None]                                              # :102
+    k_beta = k * beta[..., None]                                              # :103
+    r = lambda t: t.reshape(Nv, nc, C, t.shape[-1])  # noqa: E731
+    q, k, v, k_beta, v_beta = r(q), r(k), r(v), r(k_beta), r(v_beta)
+    g = g.reshape(Nv, nc, C)
+    g = _cumsum_f32(g, -1)                                                    # :114
+    decay_mask = np.tril(_exp(np.tril(g[..., :, None] - g[..., None, :])))   # :115
+    upper = np.triu(np.ones((C, C), dtype=bool), 0)                           # :110-113
+    attn = -(_mm(k_beta, np.swapaxes(k, -1, -2)) * decay_mask)                # :117
+    attn[..., upper] = 0
+    for i in range(1, C):                                                     # :118-121
+        row = attn[..., i, :i].copy()
+        sub = attn[..., :i, :i].copy()
+        attn[..., i, :i] = row + (row[..., :, None] * sub).sum(-2)
+    attn = attn + np.eye(C, dtype=np.float32)                                 # :122
+    value = _mm(attn, v_beta)                                                 # :123
+    k_cumdecay = _mm(attn, k_beta * _exp(g)[..., None])                       # :124
+    cur = state.astype(np.float32)
+    out = np.zeros_like(value)
+    strict_upper = np.triu(np.ones((C, C), dtype=bool), 1)                    # :131-134
+    for i in range(nc):                                                       # :136-150
+        qi, ki, vi = q[:, i], k[:, i], value[:, i]
+        a = _mm(qi, np.swapaxes(ki, -1, -2)) * decay_mask[:, i]
+        a[:, strict_upper] = 0
+        v_prime = _mm(k_cumdecay[:, i], cur)
+        vn = vi - v_prime
+        inter = _mm(qi * _exp(g[:, i])[..., None], cur)
+        out[:, i] = inter + _mm(a, vn)
+        cur = cur * _exp(g[:, i, -1])[:, None, None] + _mm(
+            np.swapaxes(ki * _exp(g[:, i, -1, None] - g[:, i])[..., None], -1, -2), vn)
+    out = out.reshape(Nv, Sp, -1)[:, :S]
+    return np.ascontiguousarray(out.transpose(1, 0, 2)), cur
+
+
+# ---- chunk output in the fla layout (the chunk-output kernel's specification) --------
+
+def chunk_o(q, k, v_new, h, g=None, scale=None, cu_seqlens=None):
+    """o ``[B,T,H,V]`` (bf16 values) from q, k ``[B,T,HK,K]``, v_new
+    ``[B,T,H,V]``, h ``[B,NT,H,K,V]`` (the state before each chunk, ``[K, V]``
+    per head) and the chunk-local cumulative gate g ``[B,T,H]``:
+    attn_inter = bf16(q' h) with q' = bf16(q * scale * exp(g))
+    (benchmark.py:77-79, :129), then stage 3 (benchmark.py:145-175)."""
+    q, k, v_new, h = (np.asarray(x, dtype=np.float32) for x in (q, k, v_new, h))
+    B, T, HK, K = q.shape
+    H, V = v_new.shape[2], v_new.shape[3]
+    rep = H // HK
+    scale = np.float32(1.0 / K ** 0.5 if scale is None else scale)
+    g = np.zeros((B, T, H), dtype=np.float32) if g is None else np.asarray(g, dtype=np.float32)
+    o = np.zeros((B, T, H, V), dtype=np.float32)
+    if cu_seqlens is None:
+        spans = [(b, t0, min(C, T - t0), (b, t0 // C)) for b in range(B) for t0 in range(0, T, C)]
+    else:
+        cu = [int(x) for x in cu_seqlens]
+        spans, row = [], 0
+        for n in range(len(cu) - 1):
+            for t0 in range(cu[n], cu[n + 1], C):
+                spans.append((0, t0, min(C, cu[n + 1] - t0), (0, row)))
+                row += 1
+    lower = np.tril(np.ones((C, C), dtype=bool), 0)
+    for b, t0, L, (hb, hc) in spans:
+        qh = np.repeat(q[b, t0:t0 + L], rep, axis=1).transpose(1, 0, 2)      # [H, L, K]
+        kh = np.repeat(k[b, t0:t0 + L], rep, axis=1).transpose(1, 0, 2)
+        vn = v_new[b, t0:t0 + L].transpose(1, 0, 2)                           # [H, L, V]
+        gc = g[b, t0:t0 + L].T                                                # [H, L]
+        qp = bf16r((qh * scale) * _exp(gc)[..., None])
+        inter = bf16r(_mm(qp, h[hb, hc]))
+        qkt = bf16r(_mm(qh, kh.transpose(0, 2, 1)))
+        lw = lower[:L, :L]
+        decay = _exp((gc[:, :, None] - gc[:, None, :]) * lw) * lw
+        inner = bf16r(_mm(bf16r((qkt * scale) * decay), vn))
+        o[b, t0:t0 + L] = bf16r(inter + inner).transpose(1, 0, 2)
+    return o
+
+
+# ---- the reference's three-party check (tests/assets/impl/compare.py) -------------------
+
+_MIN_ERR = 1e-3                # compare.py:23
+_ERR_THRESHOLD = 2.0 ** -8     # :24
+_SMALL_VALUE = 2.0 ** -10      # :25
+_SMALL_VALUE_ATOL = 1e-16      # :26
+CV_MAX_RE, CV_AVER_RE, CV_RMSE, CV_SMALL_VAL = 5.0, 1.5, 1.5, 2.0  # :28-31
+
+
+def _metrics(actual, golden):
+    rel = np.abs(actual - golden) / (np.abs(golden) + _MIN_ERR)
+    small = np.abs(golden) < _SMALL_VALUE
+    n_small = int(small.sum())
+    err = small & (np.abs(golden - actual) > _SMALL_VALUE_ATOL)
+    smra = (int(err.sum()) / n_small) if n_small else 0.0
+    return float(rel.max(initial=0.0)), float(rel.mean()) if rel.size else 0.0, \
+        float(np.sqrt(np.mean((actual - golden) ** 2))) if rel.size else 0.0, smra
+
+
+def _ratio(num, den):
+    if den is None or den == 0:
+        return 1.0 if num == 0 else float("inf")
+    return float(num / max(den, _ERR_THRESHOLD))
+
+
+def cross_check(actual, golden, bench) -> dict:
+    """compare.py:94-210: error ratios (ours / the bf16 benchmark's) against
+    the fp32 golden; passes when every ratio is under its threshold, or when
+    our max relative error is below 2**-7."""
+    g = np.asarray(golden, dtype=np.float32).reshape(-1)
+    t = np.asarray(actual, dtype=np.float32).reshape(-1)
+    b = np.asarray(bench, dtype=np.float32).reshape(-1)
+    mt, at, rt, st = _metrics(t, g)
+    mb, ab, rb, sb = _metrics(b, g)
+    r = dict(mare_ratio=_ratio(mt, mb), mere_ratio=_ratio(at, ab), rmse_ratio=_ratio(rt, rb),
+             smra_ratio=_ratio(st, sb), max_re=mt, max_re_bench=mb, avg_re=at, avg_re_bench=ab)
+    passed = (r["mare_ratio"] < CV_MAX_RE and r["mere_ratio"] < CV_AVER_RE and r["rmse_ratio"] < CV_RMSE
+              and r["smra_ratio"] < CV_SMALL_VAL)
+    if not passed and mt < 2.0 ** -7:
+        passed = True
+    r["pass"] = passed
+    return r

@@ -28,11 +28,15 @@ BF, F32, I64 = torch.bfloat16, torch.float32, torch.int64
 
 def test_library_loads_and_exports_every_declared_symbol():
     lib = _lib.load()
-    header = (ROOT / "include" / "cgdr_fwd_h.h").read_text()
-    declared = set(re.findall(r"^(?:cgdrStatus|void|int32_t|const char\*)\s+(cgdr\w+)\(", header, re.MULTILINE))
-    assert declared == set(_lib.EXPORTS), declared ^ set(_lib.EXPORTS)
-    for sym in declared:
-        assert hasattr(lib, sym), sym
+    headers = sorted((ROOT / "include").glob("*.h"))
+    assert {h.name for h in headers} == set(_lib.EXPORTS_BY_HEADER)
+    for hdr in headers:
+        declared = set(re.findall(r"^(?:cgdrStatus|void|int32_t|int64_t|const char\*)\s+(cgdr\w+)\(",
+                                  hdr.read_text(), re.MULTILINE))
+        expected = set(_lib.EXPORTS_BY_HEADER[hdr.name])
+        assert declared == expected, (hdr.name, declared ^ expected)
+        for sym in declared:
+            assert hasattr(lib, sym), sym
     assert lib.cgdrGetAbiVersion() == 1
 
 
