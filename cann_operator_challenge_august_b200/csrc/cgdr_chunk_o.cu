@@ -25,6 +25,19 @@ namespace {
 
 constexpr uint32_t kMagicO = 0xC6D20C01u;
 constexpr uint64_t kHeader = 256;
+constexpr int kStagesO = 2;
+
+// SMs of the current device (148 on B200); the plan falls back to that
+// figure when no device is visible (phase 1 runs on hosts without a GPU).
+int64_t sm_count()
+{
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess && cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess &&
+        n > 0)
+        return n;
+    cudaGetLastError();
+    return 148;
+}
 
 cgdrStatus build_o(const cgdrTensor* q, const cgdrTensor* k, const cgdrTensor* v, const cgdrTensor* h,
                    const cgdrTensor* g, const cgdrTensor* cu, const cgdrTensor* ci, double scale, int64_t chunk_size,
@@ -107,11 +120,9 @@ cgdrStatus build_o(const cgdrTensor* q, const cgdrTensor* k, const cgdrTensor* v
     const int32_t tmo = opt && opt->wait_timeout_ms > 0 ? opt->wait_timeout_ms : 2000;
     p.timeout_ns = static_cast<uint64_t>(tmo) * 1000000ull;
     ex->tq = *q; ex->tk = *k; ex->tv = *v; ex->th = *h; ex->to = *o;
-    ex->grid = rows * H * p.n_vtiles;
-    if (ex->grid >= (int64_t(1) << 31)) {
-        delete ex;
-        return fail(CGDR_STATUS_UNSUPPORTED, "too many chunks for one launch");
-    }
+    p.n_tiles = rows * H * p.n_vtiles;
+    // persistent: one CTA per SM (or per tile when there are fewer tiles)
+    ex->grid = p.n_tiles < sm_count() ? p.n_tiles : sm_count();
     *ws_size = kHeader;
     *out = ex;
     g_err[0] = '\0';
@@ -121,7 +132,6 @@ cgdrStatus build_o(const cgdrTensor* q, const cgdrTensor* k, const cgdrTensor* v
 cgdrStatus build_maps_o(const cgdrChunkOExecutor* ex, ChunkOMaps* m)
 {
     const ChunkOParams& p = ex->p;
-    const int vt = p.V / p.n_vtiles;
     cgdrStatus st;
     {
         const cgdrTensor& t = ex->tq;
@@ -148,21 +158,14 @@ cgdrStatus build_maps_o(const cgdrChunkOExecutor* ex, ChunkOMaps* m)
         const uint32_t box[5] = {64, static_cast<uint32_t>(p.K), 1, 1, 1};
         if ((st = make_map(&m->h, t.data, 5, size, stride, box, "h"))) return st;
     }
-    {
-        const cgdrTensor& t = ex->to;
-        const int64_t size[4] = {p.V, p.H, p.T, p.B}, stride[4] = {1, t.strides[2], t.strides[1], t.strides[0]};
-        const uint32_t box[4] = {64, 1, 64, 1};
-        if ((st = make_map(&m->o, t.data, 4, size, stride, box, "o"))) return st;
-    }
-    (void)vt;
     return CGDR_STATUS_SUCCESS;
 }
 
 template <int K_, int VT>
 cudaError_t launch_o(const ChunkOArgs& args, int64_t grid, cudaStream_t stream)
 {
-    using Cfg = ChunkOConfig<K_, VT>;
-    auto kern = chunk_o_tc_kernel<K_, VT>;
+    using Cfg = ChunkOConfig<K_, VT, kStagesO>;
+    auto kern = chunk_o_tc_kernel<K_, VT, kStagesO>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
     if (e != cudaSuccess) return e;
     kern<<<static_cast<unsigned>(grid), Cfg::kThreads, Cfg::kSmemBytes, stream>>>(args);
