@@ -2,8 +2,9 @@
 forward hidden-state recurrence of Gated DeltaNet prefill.
 
 The compute is a CUDA library with a C ABI (include/cgdr_fwd_h.h for the
-recurrence, include/cgdr_chunk_o.h for the chunk output that consumes it);
-this package is its Python host side.  See :mod:`.api` and :mod:`.gdr`.
+recurrence, include/cgdr_wy.h for the WY representation that feeds it,
+include/cgdr_chunk_o.h for the chunk output that consumes it); this package
+is its Python host side.  See :mod:`.api` and :mod:`.gdr`.
 """
 
 from .api import (  # noqa: F401
@@ -15,7 +16,7 @@ from .api import (  # noqa: F401
     read_device_status,
     run,
 )
-from .gdr import ChunkGatedDeltaRuleFwdO, chunk_fwd_o  # noqa: F401
+from .gdr import ChunkGatedDeltaRuleFwdO, ChunkGatedDeltaRuleWY, chunk_fwd_o, chunk_wy_fwd  # noqa: F401
 from ._lib import CgdrError, CgdrValueError  # noqa: F401
 
 __all__ = [
@@ -28,6 +29,8 @@ __all__ = [
     "run",
     "ChunkGatedDeltaRuleFwdO",
     "chunk_fwd_o",
+    "ChunkGatedDeltaRuleWY",
+    "chunk_wy_fwd",
     "CgdrError",
     "CgdrValueError",
 ]

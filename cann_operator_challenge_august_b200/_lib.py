@@ -52,6 +52,11 @@ EXPORTS_BY_HEADER = {
         "cgdrDestroyChunkOExecutor",
         "cgdrChunkOGridSize",
     ),
+    "cgdr_wy.h": (
+        "cgdrChunkGatedDeltaRuleWYGetWorkspaceSize",
+        "cgdrChunkGatedDeltaRuleWY",
+        "cgdrDestroyWyExecutor",
+    ),
 }
 EXPORTS = tuple(sym for syms in EXPORTS_BY_HEADER.values() for sym in syms)
 
@@ -80,6 +85,10 @@ class CgdrFwdHOptions(ctypes.Structure):
 
 
 class CgdrChunkOOptions(ctypes.Structure):
+    _fields_ = [("wait_timeout_ms", ctypes.c_int32), ("reserved", ctypes.c_int32 * 7)]
+
+
+class CgdrWyOptions(ctypes.Structure):
     _fields_ = [("wait_timeout_ms", ctypes.c_int32), ("reserved", ctypes.c_int32 * 7)]
 
 
@@ -140,6 +149,13 @@ def load() -> ctypes.CDLL:
     lib.cgdrDestroyChunkOExecutor.restype = None
     lib.cgdrChunkOGridSize.argtypes = [ctypes.c_void_p]
     lib.cgdrChunkOGridSize.restype = ctypes.c_int64
+    lib.cgdrChunkGatedDeltaRuleWYGetWorkspaceSize.argtypes = (
+        [T] * 6 + [ctypes.c_int64] + [T] * 3 + [ctypes.POINTER(CgdrWyOptions), u64p, exp])
+    lib.cgdrChunkGatedDeltaRuleWYGetWorkspaceSize.restype = ctypes.c_int
+    lib.cgdrChunkGatedDeltaRuleWY.argtypes = [ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p, ctypes.c_void_p]
+    lib.cgdrChunkGatedDeltaRuleWY.restype = ctypes.c_int
+    lib.cgdrDestroyWyExecutor.argtypes = [ctypes.c_void_p]
+    lib.cgdrDestroyWyExecutor.restype = None
     lib.cgdrGetAbiVersion.argtypes = []
     lib.cgdrGetAbiVersion.restype = ctypes.c_int32
     _lib = lib

@@ -1,10 +1,15 @@
 """Python front ends of the stages around the hidden-state recurrence, over
-the C ABI in include/cgdr_chunk_o.h.
+the C ABI in include/cgdr_chunk_o.h and include/cgdr_wy.h.
 
 * :class:`ChunkGatedDeltaRuleFwdO` -- two-phase call of the chunk output
   (workspace query, then launch into a caller-owned ``o``).
 * :func:`chunk_fwd_o` -- allocate-and-call form with the argument set of the
   fla ``chunk_fwd_o`` wrapper.
+* :class:`ChunkGatedDeltaRuleWY` / :func:`chunk_wy_fwd` -- the WY
+  representation that produces the recurrence's w, u and chunk-local
+  cumulative gate from k, v, beta and the per-token gate (the reference's
+  stage 1, ref/chunk_gated_delta_rule/tests/pytest/
+  chunk_gated_delta_rule_benchmark.py:55-83).
 
 The chunk output is the consumer of ``chunk_gated_delta_rule_fwd_h``'s ``h``
 and ``v_new``: per 64-token chunk, ``o = q' h[c] + P v_new`` with
@@ -99,3 +104,73 @@ def chunk_fwd_o(
         if status:
             raise RuntimeError(f"device status 0x{status:x}")
     return o
+
+
+class ChunkGatedDeltaRuleWY:
+    """Two-phase WY representation: ``op = ChunkGatedDeltaRuleWY(k, v, beta,
+    g, cu_seqlens, chunk_indices, chunk_size, w, u, g_cum)`` validates and
+    plans; ``op(workspace)`` enqueues the kernel on the current stream."""
+
+    def __init__(self, k, v, beta, g, cu_seqlens, chunk_indices, chunk_size, w, u, g_cum, *, wait_timeout_ms=0):
+        lib = _lib.load()
+        self._keep = (k, v, beta, g, cu_seqlens, chunk_indices, w, u, g_cum)
+        ws = ctypes.c_uint64(0)
+        ex = ctypes.c_void_p(None)
+        opt = _lib.CgdrWyOptions(wait_timeout_ms=int(wait_timeout_ms))
+        descs = [_desc(x) for x in (k, v, beta, g, cu_seqlens, chunk_indices)]
+        outs = [_desc(x) for x in (w, u, g_cum)]
+        st = lib.cgdrChunkGatedDeltaRuleWYGetWorkspaceSize(
+            *[ctypes.byref(d) for d in descs], int(chunk_size), *[ctypes.byref(d) for d in outs], ctypes.byref(opt),
+            ctypes.byref(ws), ctypes.byref(ex))
+        _lib.check(st, "cgdrChunkGatedDeltaRuleWYGetWorkspaceSize")
+        self._ex = ex
+        self.workspace_size = int(ws.value)
+
+    def __call__(self, workspace: torch.Tensor, stream: int | None = None) -> None:
+        if self._ex is None:
+            raise RuntimeError("executor already consumed")
+        ex, self._ex = self._ex, None
+        if stream is None:
+            stream = _stream_handle(workspace.device)
+        st = _lib.load().cgdrChunkGatedDeltaRuleWY(
+            ctypes.c_void_p(workspace.data_ptr()), workspace.numel() * workspace.element_size(), ex,
+            ctypes.c_void_p(stream))
+        _lib.check(st, "cgdrChunkGatedDeltaRuleWY")
+
+    def __del__(self):
+        if getattr(self, "_ex", None) is not None and _lib._lib is not None:
+            _lib._lib.cgdrDestroyWyExecutor(self._ex)
+            self._ex = None
+
+
+def chunk_wy_fwd(
+    k: torch.Tensor,
+    v: torch.Tensor,
+    beta: torch.Tensor,
+    g: torch.Tensor | None = None,
+    cu_seqlens: torch.LongTensor | None = None,
+    chunk_size: int = CHUNK_SIZE,
+    chunk_indices: torch.Tensor | None = None,
+    *,
+    check_device_status: bool = False,
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """WY representation: returns ``(w [B,T,H,K], u [B,T,H,V], g_cum [B,T,H])``
+    from k ``[B,T,Hg,K]``, v ``[B,T,H,V]``, beta ``[B,T,H]`` (bf16) and the
+    per-token log gate g ``[B,T,H]`` (fp32, optional).  ``g_cum`` is the
+    chunk-local cumulative gate that the recurrence and the chunk output take
+    as their ``g``."""
+    _require_cuda(k, v, beta, g, cu_seqlens, chunk_indices)
+    if cu_seqlens is not None and chunk_indices is None:
+        chunk_indices = prepare_chunk_indices(cu_seqlens, chunk_size)
+    B, T, H = v.shape[0], v.shape[1], v.shape[2]
+    w = k.new_empty(B, T, H, k.shape[3])
+    u = torch.empty_like(v)
+    g_cum = torch.empty(B, T, H, dtype=torch.float32, device=v.device)
+    op = ChunkGatedDeltaRuleWY(k, v, beta, g, cu_seqlens, chunk_indices, chunk_size, w, u, g_cum)
+    ws = torch.empty(max(op.workspace_size, 256), dtype=torch.uint8, device=v.device)
+    op(ws)
+    if check_device_status:
+        status = read_device_status(ws)
+        if status:
+            raise RuntimeError(f"device status 0x{status:x}")
+    return w, u, g_cum

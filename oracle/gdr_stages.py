@@ -304,6 +304,38 @@ def chunk_o(q, k, v_new, h, g=None, scale=None, cu_seqlens=None):
     return o
 
 
+# ---- WY representation in the fla layout (the WY kernel's specification) ---------------
+
+def wy(k, v, beta, g=None, cu_seqlens=None):
+    """w ``[B,T,H,K]``, u ``[B,T,H,V]`` (bf16 values) and the chunk-local
+    cumulative gate ``[B,T,H]`` from k ``[B,T,HK,K]``, v ``[B,T,H,V]``,
+    beta and the per-token gate g ``[B,T,H]``: stage 1 of the reference per
+    sequence (benchmark.py:55-83), with w = -k_cumdecay."""
+    k, v, beta = (np.asarray(x, dtype=np.float32) for x in (k, v, beta))
+    B, T, HK, K = k.shape
+    H, V = v.shape[2], v.shape[3]
+    rep = H // HK
+    g = np.zeros((B, T, H), np.float32) if g is None else np.asarray(g, dtype=np.float32)
+    w = np.zeros((B, T, H, K), np.float32)
+    u = np.zeros((B, T, H, V), np.float32)
+    gc = np.zeros((B, T, H), np.float32)
+    if cu_seqlens is None:
+        spans = [(b, 0, T) for b in range(B)]
+    else:
+        cu = [int(x) for x in cu_seqlens]
+        spans = [(0, cu[n], cu[n + 1]) for n in range(len(cu) - 1)]
+    for b, bos, eos in spans:
+        S = eos - bos
+        if S <= 0:
+            continue
+        ks = np.repeat(k[b, bos:eos], rep, axis=1)
+        s1 = stage1(ks, ks, v[b, bos:eos], g[b, bos:eos], beta[b, bos:eos], 1.0)
+        w[b, bos:eos] = -s1["k_cumdecay"][:, :S].transpose(1, 0, 2)
+        u[b, bos:eos] = s1["v_inner"][:, :S].transpose(1, 0, 2)
+        gc[b, bos:eos] = s1["g_cum"][:, :S].T
+    return w, u, gc
+
+
 # ---- the reference's three-party check (tests/assets/impl/compare.py) -------------------
 
 _MIN_ERR = 1e-3                # compare.py:23

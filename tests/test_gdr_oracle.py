@@ -133,3 +133,17 @@ def test_cross_check_restatement(name):
     rng = np.random.default_rng(0)
     bad = bench + 0.05 * np.abs(bench).max() * rng.standard_normal(bench.shape).astype(np.float32)
     assert not G.cross_check(bad, golden, bench)["pass"]
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_wy_fla_layout_restatement(name):
+    """The fla-layout WY wrapper (the WY kernel's specification) reproduces the
+    reference's stage-1 outputs on its own inputs."""
+    z = load(name)
+    lens = z["seq_lens"]
+    cu = np.concatenate([[0], np.cumsum(lens)])
+    g = f32(z["g"])[None] if "g" in z else None
+    w, u, gc = G.wy(f32(z["k"])[None], f32(z["v"])[None], f32(z["beta"])[None], g, cu)
+    for got, ref, what in ((w, z["w"], "w"), (u, z["u"], "u"), (gc, z["g_cum"], "g_cum")):
+        eq, mx = agreement(got, f32(ref))
+        assert eq >= 0.995 and mx <= ULP, (what, eq, mx)
