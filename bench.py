@@ -362,14 +362,17 @@ def main() -> int:
     ap.add_argument("--v-tile", type=int, default=0)
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--op", choices=["fwd_h", "chunk_o"], default="fwd_h",
-                    help="fwd_h: the recurrence (the headline); chunk_o: the chunk output that consumes it")
+    ap.add_argument("--op", choices=["fwd_h", "chunk_o", "wy"], default="fwd_h",
+                    help="fwd_h: the recurrence (the headline); chunk_o: the chunk output that consumes it; "
+                         "wy: the WY representation that feeds it")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     cfg = CONFIGS[args.config]
     if args.op == "chunk_o" and args.impl == "ours":
         return main_chunk_o(args)
+    if args.op == "wy" and args.impl == "ours":
+        return main_stage(args)
 
     if args.impl == "reference":
         world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -655,6 +658,157 @@ def main_chunk_o(args) -> int:
                          else "fallback",
                          "algorithmic_bytes_per_launch": nbytes, "launch_ms": per_launch_ms,
                          "traffic": load_traffic(args.config, "chunk_o"), "kernel": "chunk_o"},
+            "clocks": clk,
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": e2e_ms},
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    return 0
+
+
+def wy_bytes(c):
+    """Algorithmic bytes of one WY launch: k, v, beta, g read once; w, u, g_c
+    written once."""
+    B, T, H, HK, K, V = c["B"], c["T"], c["H"], c["HK"], c["K"], c["V"]
+    return B * T * (HK * K * 2 + H * V * 2 + H * 2 + H * 4 + H * K * 2 + H * V * 2 + H * 4)
+
+
+def gen_wy_inputs(c, seed, device):
+    """k L2-normalised, v ~ randn, beta ~ U(0, 1), g ~ U(-1, 0): the reference
+    operator's input constraints (ref/chunk_gated_delta_rule/tests/assets/impl/inputs.py)."""
+    import torch
+    g0 = torch.Generator(device=device).manual_seed(seed)
+    B, T, H, HK, K, V = c["B"], c["T"], c["H"], c["HK"], c["K"], c["V"]
+    k = torch.nn.functional.normalize(torch.randn(B, T, HK, K, device=device, generator=g0), dim=-1).to(torch.bfloat16)
+    v = torch.randn(B, T, H, V, device=device, generator=g0).to(torch.bfloat16)
+    beta = torch.rand(B, T, H, device=device, generator=g0).clamp(1e-6, 1 - 1e-6).to(torch.bfloat16)
+    g = -torch.rand(B, T, H, device=device, generator=g0)
+    return k, v, beta, g
+
+
+def cpu_wy_rate(c, k, v, beta, g, budget_s):
+    """The WY oracle (numpy) on the first chunks of batch row 0, all heads,
+    scaled to the whole job."""
+    from oracle import gdr_stages as G
+
+    def timed(nc):
+        T = 64 * nc
+        a = [t[:1, :T].float().cpu().numpy() for t in (k, v, beta, g)]
+        t0 = time.perf_counter()
+        G.wy(*a)
+        return time.perf_counter() - t0
+
+    t1 = timed(1)
+    NT = (c["T"] + 63) // 64
+    nc = int(max(1, min(NT, budget_s / max(t1, 1e-4))))
+    dt = timed(nc)
+    rate = c["B"] * c["T"] * (nc / dt) / (c["B"] * NT)
+    threads = int(os.environ.get("OMP_NUM_THREADS", "0") or 0) or len(os.sched_getaffinity(0))
+    desc = f"{nc} of {c['B'] * NT} (batch row, chunk) tiles, all {c['H']} heads ({dt:.2f} s), scaled to the whole job"
+    return rate, desc, threads
+
+
+def main_stage(args) -> int:
+    """--op wy: the WY representation that produces fwd_h's w, u and
+    cumulative gate, on the fixed-length configurations."""
+    import torch
+    import cann_operator_challenge_august_b200 as cg
+
+    world, rank, local = dist_setup()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    c = shard(CONFIGS[args.config], world, rank)
+    if "seqs" in c or c["K"] > 128 or c["V"] > 128:
+        raise SystemExit("--op wy runs the fixed-length configurations with K, V <= 128")
+    k, v, beta, g = gen_wy_inputs(c, 3000 + rank, dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        return cg.chunk_wy_fwd(k, v, beta, g)
+
+    for _ in range(args.warmup):
+        out = step()
+    torch.cuda.synchronize()
+    uuid = None
+    try:
+        uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:
+        pass
+    clocks = ClockSampler(uuid)
+    clocks.start()
+    time.sleep(0.3)
+    barrier(world)
+    torch.cuda.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * args.steps)]
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_stop = torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for i in range(args.steps):
+        ev[2 * i].record(stream)
+        out = step()
+        ev[2 * i + 1].record(stream)
+    t_stop.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    clk = clocks.stop()
+    elapsed_ms = max_over_ranks(t_start.elapsed_time(t_stop), world)
+    per_launch_ms = max_over_ranks(sum(ev[2 * i].elapsed_time(ev[2 * i + 1]) for i in range(args.steps)) / args.steps,
+                                   world)
+    ms_per_step = elapsed_ms / args.steps
+    tokens_per_step = c["B"] * c["T"] * world
+    value = tokens_per_step / (ms_per_step / 1000.0)
+
+    host = [t.cpu().pin_memory() for t in (k, v, beta, g)]
+    h2d = sum(t.numel() * t.element_size() for t in host)
+    host_out = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in out]
+    d2h = sum(t.numel() * t.element_size() for t in host_out)
+
+    def e2e_step():
+        d = [t.to(dev, non_blocking=True) for t in host]
+        for dst, src in zip(host_out, cg.chunk_wy_fwd(*d)):
+            dst.copy_(src, non_blocking=True)
+
+    e2e_ms = e2e_value = None
+    if args.e2e_steps > 0:
+        e2e_step()
+        torch.cuda.synchronize()
+        barrier(world)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.e2e_steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = max_over_ranks(e0.elapsed_time(e1), world) / args.e2e_steps
+        e2e_value = tokens_per_step / (e2e_ms / 1000.0)
+
+    nbytes = wy_bytes(c)
+    peak, peak_kind = load_peaks()
+    achieved = nbytes / (per_launch_ms / 1000.0) / 1e9
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rate, desc, threads = cpu_wy_rate(c, k, v, beta, g, 10.0)
+        cpu = {"value": rate, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": desc}
+    if rank == 0:
+        line = {
+            "metric": "wy tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+            "scaling": c["scaling"], "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded, generated on device per rank, the reference operator's input ranges)",
+            "config": dict(config_block(args.config, c, world, nbytes),
+                           workload=f"{args.config}: WY representation bf16 B={c['B']} T={c['T']} H={c['H']} "
+                                    f"K={c['K']} V={c['V']} chunk=64 (k, v, beta, g in; w, u, g_c out)"),
+            "gpu_launches": args.steps,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                         else "fallback",
+                         "algorithmic_bytes_per_launch": nbytes, "launch_ms": per_launch_ms,
+                         "traffic": load_traffic(args.config, "wy"), "kernel": "wy"},
             "clocks": clk,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": e2e_ms},

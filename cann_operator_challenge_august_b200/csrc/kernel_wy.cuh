@@ -15,6 +15,12 @@
 // 16 x 16 diagonal blocks, then block forward substitution for the blocks
 // below the diagonal, T_ij = -T_ii sum_{m=j}^{i-1} A_im T_mj, in fp32.
 //
+// The reference rounds k' = beta * exp(g_c) * k and v' = beta * v to bf16 and
+// multiplies them by bf16(T).  Here the row factors move onto T's columns:
+// W = bf16(T diag(beta e^g_c)) . k and U = bf16(T diag(beta)) . v, so k and v
+// go to the tensor cores as TMA delivered them; the two orders differ at the
+// bf16 rounding of the operands.
+//
 // Persistent kernel, one CTA per SM walking tiles (chunk row, value head)
 // blockIdx.x, blockIdx.x + gridDim.x, ...  Warp roles (352 threads):
 //   warp 0      TMA producer: k and v of a tile into a STAGES-deep ring;
@@ -23,13 +29,18 @@
 //               W's first 64 columns and read before W's product overwrites it);
 //   warp 2      gate loader: beta and g of the tile (plain loads), the fp64
 //               cumulative sum, the g_c output, both into the stage;
-//   warps 3-10  epilogue: warp w reads TMEM lanes 32(w%4).. (rows 16(w%4)..+15
-//               of an M=64 accumulator) and half of the columns ((w-3)/4).
-// Per tile (stage s, accumulator set a):
+//   warps 3-10  two epilogue groups of four warps (one per TMEM lane quadrant:
+//               warp w reads lanes 32(w%4).., rows 16(w%4)..+15 of an M=64
+//               accumulator).  Group g takes the tiles of accumulator set g
+//               (every other tile), so two tiles are solved at once, each group
+//               with its own scratch and named barrier.
+// Per tile (stage s, accumulator set a = group):
 //   MMA   KK[a] = k k^T                       M=64 N=64 K=K (both K-major)
-//   epi   A; k' = beta e^g k and v' = beta v in place; T; T -> bf16 tile T[a]
-//   MMA   W[a] = T k' ; U[a] = T v'           M=64 N=K / V K=64 (B MN-major)
-//   epi   w, u = bf16 -> swizzled staging -> coalesced 16-byte stores
+//   epi   A; T (diagonal 16 x 16 blocks one per warp, then the blocks below the
+//         diagonal); T' = bf16(T diag(beta e^g_c)), T'' = bf16(T diag(beta))
+//   MMA   W[a] = T' k ; U[a] = T'' v          M=64 N=K / V K=64 (B MN-major)
+//   epi   w, u = bf16 from TMEM rows (32x32b loads) -> 16-byte stores
+// The MMA warp issues KK of tile i+1 before it waits for tile i's T.
 // Every wait is bounded and no role leaves early (see kernel_chunk_o.cuh).
 #pragma once
 
@@ -85,15 +96,13 @@ struct WyConfig {
     static constexpr int kOffV = kTileK;
     static constexpr int kOffBeta = kTileK + kTileV;  // 64 fp32
     static constexpr int kOffGc = kOffBeta + 256;     // 64 fp32 (cumulative gate)
-    static constexpr int kStageBytes = (kOffGc + 256 + 1023) / 1024 * 1024;
-    static constexpr int kOffT = STAGES * kStageBytes;  // [2] bf16 T tiles [64][64], 128-byte swizzle
+    static constexpr int kOffD = kOffGc + 256;        // 64 fp32: beta * exp(g_c), T' column factors
+    static constexpr int kStageBytes = (kOffD + 256 + 1023) / 1024 * 1024;
+    static constexpr int kOffT = STAGES * kStageBytes;  // [2 sets][T', T''] bf16 [64][64], 128-byte swizzle
     static constexpr int kLd = 68;                       // fp32 row stride of A and Tf
-    static constexpr int kOffA = kOffT + 2 * 8192;       // fp32 A [64][kLd]
-    static constexpr int kOffTf = kOffA + 64 * kLd * 4;  // fp32 T [64][kLd]
-    static constexpr int kOffY = kOffTf + 64 * kLd * 4;  // fp32 [3][16][16] block products
-    static constexpr int kOffOutW = (kOffY + 3 * 256 * 4 + 1023) / 1024 * 1024;  // staging [64][K]
-    static constexpr int kOffOutU = kOffOutW + kTileK;                            // staging [64][V]
-    static constexpr int kOffBar = kOffOutU + kTileV;
+    static constexpr int kScratch = 2 * 64 * kLd * 4 + 6 * 256 * 4;  // A, Tf, Y [6][16][16] of a group
+    static constexpr int kOffScratch = kOffT + 4 * 8192;             // [2 groups]
+    static constexpr int kOffBar = (kOffScratch + 2 * kScratch + 1023) / 1024 * 1024;
     static constexpr int kNumBars = 2 * STAGES + 9;
     static constexpr int kUsed = kOffBar + kNumBars * 8 + 16;
     static constexpr int kSmemBytes = (kUsed + 1024 > 120 * 1024) ? kUsed + 1024 : 120 * 1024;
@@ -139,7 +148,8 @@ __device__ __forceinline__ WyTile wy_tile(const WyParams& p, int64_t tile)
     return t;
 }
 
-__device__ __forceinline__ void wy_epi_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+// named barrier of epilogue group g (ids 1 and 2, 128 threads each)
+__device__ __forceinline__ void wy_group_bar(int g) { asm volatile("bar.sync %0, 128;" ::"r"(1 + g) : "memory"); }
 
 template <int K_, int V_, int STAGES>
 __global__ void __launch_bounds__(352, 1) wy_tc_kernel(const __grid_constant__ WyArgs args)
@@ -170,9 +180,9 @@ __global__ void __launch_bounds__(352, 1) wy_tc_kernel(const __grid_constant__ W
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&kk_full[a], 1);
-            mbar_init(&t_ready[a], Cfg::kEpiWarps);
+            mbar_init(&t_ready[a], 4);  // the four warps of group a
             mbar_init(&wu_full[a], 1);
-            mbar_init(&acc_empty[a], Cfg::kEpiWarps);
+            mbar_init(&acc_empty[a], 4);
         }
         mbar_init(mma_drain, 1);
         *abort_flag = 0;
@@ -259,10 +269,13 @@ __global__ void __launch_bounds__(352, 1) wy_tc_kernel(const __grid_constant__ W
             const float c0 = static_cast<float>(excl + x0), c1 = static_cast<float>(incl);
             float* sb = reinterpret_cast<float*>(smem + s * Cfg::kStageBytes + Cfg::kOffBeta);
             float* sg = reinterpret_cast<float*>(smem + s * Cfg::kStageBytes + Cfg::kOffGc);
+            float* sd = reinterpret_cast<float*>(smem + s * Cfg::kStageBytes + Cfg::kOffD);
             sb[2 * lane] = be[0];
             sb[2 * lane + 1] = be[1];
             sg[2 * lane] = c0;
             sg[2 * lane + 1] = c1;
+            sd[2 * lane] = __fmul_rn(be[0], expf(c0));
+            sd[2 * lane + 1] = __fmul_rn(be[1], expf(c1));
             if (p.g_cum) {
                 if (2 * lane < t.len) p.g_cum[t.b * p.c_sb + (t.t0 + 2 * lane) * p.c_st + t.hv * p.c_sh] = c0;
                 if (2 * lane + 1 < t.len) p.g_cum[t.b * p.c_sb + (t.t0 + 2 * lane + 1) * p.c_st + t.hv * p.c_sh] = c1;
@@ -273,8 +286,33 @@ __global__ void __launch_bounds__(352, 1) wy_tc_kernel(const __grid_constant__ W
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
+            // W and U of tile j (stage s, set a) once its T' / T'' are ready
+            auto issue_wu = [&](int64_t j) -> bool {
+                const int s = static_cast<int>(j % STAGES);
+                const int a = static_cast<int>(j & 1);
+                if (!mbar_wait(&t_ready[a], static_cast<uint32_t>(j / 2) & 1, ctl, 0x20)) return false;
+                tc_fence_after();
+                const uint32_t st = sbase + s * Cfg::kStageBytes;
+                const uint32_t acc = tmem + a * Cfg::kAccStride;
+                const uint64_t tw = umma_desc_sw128(sbase + Cfg::kOffT + (2 * a) * 8192, 16, 1024);
+                const uint64_t tu = umma_desc_sw128(sbase + Cfg::kOffT + (2 * a + 1) * 8192, 16, 1024);
+                const uint64_t kb = umma_desc_sw128(st + Cfg::kOffK, 8192, 1024);
+                const uint64_t vb = umma_desc_sw128(st + Cfg::kOffV, 8192, 1024);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    tc_mma_bf16(acc, tw + static_cast<uint64_t>((kk * 32) >> 4), kb + static_cast<uint64_t>((kk * 2048) >> 4),
+                                Cfg::kIdescW, kk > 0 ? 1u : 0u);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    tc_mma_bf16(acc + Cfg::kTmemU, tu + static_cast<uint64_t>((kk * 32) >> 4),
+                                vb + static_cast<uint64_t>((kk * 2048) >> 4), Cfg::kIdescU, kk > 0 ? 1u : 0u);
+                tc_commit(&wu_full[a]);
+                tc_commit(&empty[s]);
+                return true;
+            };
             int64_t it = 0;
-            for (int64_t tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x) {
+            bool ok = true;
+            for (int64_t tile = blockIdx.x; tile < p.n_tiles && ok; tile += gridDim.x) {
                 const WyTile t = wy_tile(p, tile);
                 if (!t.ok) continue;
                 const int s = static_cast<int>(it % STAGES);
@@ -293,251 +331,231 @@ __global__ void __launch_bounds__(352, 1) wy_tc_kernel(const __grid_constant__ W
                     }
                 }
                 tc_commit(&kk_full[a]);
-                if (!mbar_wait(&t_ready[a], static_cast<uint32_t>(it / 2) & 1, ctl, 0x20)) break;
-                tc_fence_after();
-                {
-                    const uint64_t ta = umma_desc_sw128(sbase + Cfg::kOffT + a * 8192, 16, 1024);
-                    const uint64_t kb = umma_desc_sw128(st + Cfg::kOffK, 8192, 1024);
-                    const uint64_t vb = umma_desc_sw128(st + Cfg::kOffV, 8192, 1024);
-#pragma unroll
-                    for (int kk = 0; kk < 4; ++kk)
-                        tc_mma_bf16(acc, ta + static_cast<uint64_t>((kk * 32) >> 4),
-                                    kb + static_cast<uint64_t>((kk * 2048) >> 4), Cfg::kIdescW, kk > 0 ? 1u : 0u);
-#pragma unroll
-                    for (int kk = 0; kk < 4; ++kk)
-                        tc_mma_bf16(acc + Cfg::kTmemU, ta + static_cast<uint64_t>((kk * 32) >> 4),
-                                    vb + static_cast<uint64_t>((kk * 2048) >> 4), Cfg::kIdescU, kk > 0 ? 1u : 0u);
-                }
-                tc_commit(&wu_full[a]);
-                tc_commit(&empty[s]);
+                if (it >= 1) ok = issue_wu(it - 1);
                 ++it;
             }
+            if (ok && it >= 1) issue_wu(it - 1);
             tc_commit(mma_drain);
             WaitCtl drain{never_flag, p.status, p.timeout_ns};
             mbar_wait(mma_drain, 0, drain, 0x20);
         }
     } else {
         // ------------------------------------------------------------ epilogue
-        const int et = threadIdx.x - 96;     // 0..255
-        const int ew = warp - 3;             // 0..7
+        const int grp = (warp - 3) >> 2;     // group: accumulator set, every other tile
+        const int gw = (warp - 3) & 3;       // warp within the group
+        const int gt = 32 * gw + lane;       // thread within the group, 0..127
         const int qd = warp & 3;             // TMEM lane quadrant
-        const int ch = ew >> 2;              // column half
         const int ra = 16 * qd + (lane >> 2);
         const int rb = ra + 8;
         const int pc = 2 * (lane & 3);
-        float* Am = reinterpret_cast<float*>(smem + Cfg::kOffA);
-        float* Tf = reinterpret_cast<float*>(smem + Cfg::kOffTf);
-        float* Yb = reinterpret_cast<float*>(smem + Cfg::kOffY);
+        uint8_t* scratch = smem + Cfg::kOffScratch + grp * Cfg::kScratch;
+        float* Am = reinterpret_cast<float*>(scratch);
+        float* Tf = Am + 64 * Cfg::kLd;
+        float* Yb = Tf + 64 * Cfg::kLd;
         constexpr int LD = Cfg::kLd;
+        const uint32_t acc = tmem + grp * Cfg::kAccStride;
         bool ok = true;
-        int64_t it = 0;
-        WyTile prev{};
-
-        // w, u of the tile with index j (accumulator set j % 2)
-        auto output = [&](int64_t j, const WyTile& t) {
-            const int a = static_cast<int>(j & 1);
-            const uint32_t acc = tmem + a * Cfg::kAccStride + ((32u * qd) << 16);
-            if (ok) ok = mbar_wait(&wu_full[a], static_cast<uint32_t>(j / 2) & 1, ctl, 0x40);
-            ok = __all_sync(0xffffffffu, ok) != 0;
-            constexpr int kWc = K_ / 2, kUc = V_ / 2;  // columns of W / U per warp
-            uint32_t rw[kWc / 32][16], ru[kUc / 32][16];
-            if (ok) {
-                tc_fence_after();
-#pragma unroll
-                for (int cb = 0; cb < kWc / 32; ++cb)
-                    tmem_ld_16x256b_x4(acc + static_cast<uint32_t>(kWc * ch + 32 * cb), rw[cb]);
-#pragma unroll
-                for (int cb = 0; cb < kUc / 32; ++cb)
-                    tmem_ld_16x256b_x4(acc + Cfg::kTmemU + static_cast<uint32_t>(kUc * ch + 32 * cb), ru[cb]);
-                tmem_wait_ld();
-            }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&acc_empty[a]);
-            wy_epi_bar();  // staging free: every thread stored the previous tile's rows
-            uint8_t* sw = smem + Cfg::kOffOutW;
-            uint8_t* su = smem + Cfg::kOffOutU;
-            if (ok) {
-#pragma unroll
-                for (int jj = 0; jj < 4; ++jj)
-#pragma unroll
-                    for (int half = 0; half < 2; ++half) {
-                        const int i = half ? rb : ra;
-#pragma unroll
-                        for (int cb = 0; cb < kWc / 32; ++cb)
-                            *reinterpret_cast<uint32_t*>(sw + sw128_off(i, kWc * ch + 32 * cb + 8 * jj + pc, 8192)) =
-                                pack_bf16x2(__uint_as_float(rw[cb][4 * jj + 2 * half]),
-                                            __uint_as_float(rw[cb][4 * jj + 2 * half + 1]));
-#pragma unroll
-                        for (int cb = 0; cb < kUc / 32; ++cb)
-                            *reinterpret_cast<uint32_t*>(su + sw128_off(i, kUc * ch + 32 * cb + 8 * jj + pc, 8192)) =
-                                pack_bf16x2(__uint_as_float(ru[cb][4 * jj + 2 * half]),
-                                            __uint_as_float(ru[cb][4 * jj + 2 * half + 1]));
-                    }
-            }
-            wy_epi_bar();
-            if (ok) {
-                __nv_bfloat16* wr = p.w + t.b * p.w_sb + t.t0 * p.w_st + t.hv * p.w_sh;
-                __nv_bfloat16* ur = p.u + t.b * p.u_sb + t.t0 * p.u_st + t.hv * p.u_sh;
-#pragma unroll
-                for (int e = et; e < 64 * (K_ / 8); e += Cfg::kEpiThreads) {
-                    const int row = e / (K_ / 8), cc = e % (K_ / 8);
-                    if (row < t.len)
-                        *reinterpret_cast<uint4*>(wr + row * p.w_st + 8 * cc) =
-                            *reinterpret_cast<const uint4*>(sw + sw128_off(row, 8 * cc, 8192));
-                }
-#pragma unroll
-                for (int e = et; e < 64 * (V_ / 8); e += Cfg::kEpiThreads) {
-                    const int row = e / (V_ / 8), cc = e % (V_ / 8);
-                    if (row < t.len)
-                        *reinterpret_cast<uint4*>(ur + row * p.u_st + 8 * cc) =
-                            *reinterpret_cast<const uint4*>(su + sw128_off(row, 8 * cc, 8192));
-                }
-            }
-        };
-
+        int64_t it = 0;  // index among this CTA's valid tiles; this group takes it % 2 == grp
         for (int64_t tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x) {
             const WyTile t = wy_tile(p, tile);
             if (!t.ok) continue;
-            const int s = static_cast<int>(it % STAGES);
-            const int a = static_cast<int>(it & 1);
+            const int64_t my = it++;
+            if ((my & 1) != grp) continue;
+            const int s = static_cast<int>(my % STAGES);
+            const uint32_t par = static_cast<uint32_t>(my / 2) & 1;
             uint8_t* st = smem + s * Cfg::kStageBytes;
             const float* sb = reinterpret_cast<const float*>(st + Cfg::kOffBeta);
             const float* sg = reinterpret_cast<const float*>(st + Cfg::kOffGc);
-            if (ok) ok = mbar_wait(&full[s], static_cast<uint32_t>(it / STAGES) & 1, ctl, 0x40);
-            if (ok) ok = mbar_wait(&kk_full[a], static_cast<uint32_t>(it / 2) & 1, ctl, 0x40);
+            const float* sd = reinterpret_cast<const float*>(st + Cfg::kOffD);
+            if (ok) ok = mbar_wait(&full[s], static_cast<uint32_t>(my / STAGES) & 1, ctl, 0x40);
+            if (ok) ok = mbar_wait(&kk_full[grp], par, ctl, 0x40);
             ok = __all_sync(0xffffffffu, ok) != 0;
-            // ---- A = bf16(k k^T) * beta_i * exp(g_i - g_j), strictly lower, rows/cols < len
+            // ---- A = bf16(k k^T) * beta_i * exp(g_i - g_j), strictly lower, rows < len
             if (ok) {
                 tc_fence_after();
-                uint32_t kr[16];
-                tmem_ld_16x256b_x4(tmem + a * Cfg::kAccStride + ((32u * qd) << 16) + 32 * ch, kr);
-                // k' = bf16(beta * exp(g_c) * k), v' = bf16(beta * v) in place (rows past the
-                // chunk's end become 0); thread et handles row et/4, a quarter of each row
-                {
-                    const int r = et >> 2, qt = et & 3;
-                    const bool live = r < t.len;
-                    const float br = sb[r];
-                    const float fk = live ? __fmul_rn(br, expf(sg[r])) : 0.0f;
-                    constexpr int kCk = K_ / 32, kCv = V_ / 32;  // 16-byte chunks per quarter row
-#pragma unroll
-                    for (int c = 0; c < kCk; ++c) {
-                        const int idx = qt * kCk + ((c + r) & (kCk - 1));
-                        uint8_t* ptr = st + Cfg::kOffK + (idx >> 3) * 8192 + r * 128 + (idx & 7) * 16;
-                        uint4 x = *reinterpret_cast<const uint4*>(ptr);
-                        uint32_t* xs = &x.x;
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const float2 v = unpack_bf16x2(xs[e]);
-                            xs[e] = live ? pack_bf16x2(__fmul_rn(fk, v.x), __fmul_rn(fk, v.y)) : 0u;
-                        }
-                        *reinterpret_cast<uint4*>(ptr) = x;
-                    }
-#pragma unroll
-                    for (int c = 0; c < kCv; ++c) {
-                        const int idx = qt * kCv + ((c + r) & (kCv - 1));
-                        uint8_t* ptr = st + Cfg::kOffV + (idx >> 3) * 8192 + r * 128 + (idx & 7) * 16;
-                        uint4 x = *reinterpret_cast<const uint4*>(ptr);
-                        uint32_t* xs = &x.x;
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const float2 v = unpack_bf16x2(xs[e]);
-                            xs[e] = live ? pack_bf16x2(__fmul_rn(v.x, br), __fmul_rn(v.y, br)) : 0u;
-                        }
-                        *reinterpret_cast<uint4*>(ptr) = x;
-                    }
-                }
-                tmem_wait_ld();
+                uint32_t kr[2][16];
+                tmem_ld_16x256b_x4(acc + ((32u * qd) << 16), kr[0]);
+                tmem_ld_16x256b_x4(acc + ((32u * qd) << 16) + 32, kr[1]);
                 const float ba = sb[ra], bb = sb[rb], ga = sg[ra], gb = sg[rb];
+                tmem_wait_ld();
 #pragma unroll
-                for (int jj = 0; jj < 4; ++jj)
+                for (int blk = 0; blk < 2; ++blk)
 #pragma unroll
-                    for (int half = 0; half < 2; ++half) {
-                        const int i = half ? rb : ra;
-                        const float bi = half ? bb : ba, gi = half ? gb : ga;
+                    for (int jj = 0; jj < 4; ++jj)
 #pragma unroll
-                        for (int bit = 0; bit < 2; ++bit) {
-                            const int j = 32 * ch + 8 * jj + pc + bit;
-                            const float kk = round_bf16(__uint_as_float(kr[4 * jj + 2 * half + bit]));
-                            float x = 0.0f;
-                            if (j < i && i < t.len) x = __fmul_rn(__fmul_rn(kk, bi), expf(gi - sg[j]));
-                            Am[i * LD + j] = x;
+                        for (int half = 0; half < 2; ++half) {
+                            const int i = half ? rb : ra;
+                            const float bi = half ? bb : ba, gi = half ? gb : ga;
+                            const int j = 32 * blk + 8 * jj + pc;
+                            float x[2];
+#pragma unroll
+                            for (int bit = 0; bit < 2; ++bit) {
+                                const float kk = round_bf16(__uint_as_float(kr[blk][4 * jj + 2 * half + bit]));
+                                x[bit] = (j + bit < i && i < t.len)
+                                             ? __fmul_rn(__fmul_rn(kk, bi), __expf(gi - sg[j + bit]))
+                                             : 0.0f;
+                            }
+                            *reinterpret_cast<float2*>(Am + i * LD + j) = make_float2(x[0], x[1]);
                         }
-                    }
             }
-            wy_epi_bar();
-            // ---- T = (I + A)^-1: the four 16 x 16 diagonal blocks, one warp each,
-            // lane c < 16 owning column c of its block (forward substitution)
-            if (ok && ew < 4) {
-                const int b0 = 16 * ew, c = lane & 15;
-                float tcol[16];
+            tc_fence_before();
+            wy_group_bar(grp);
+            // ---- T = (I + A)^-1, diagonal blocks: warp gw owns block gw, lane c (and
+            // c + 16) column c; column-oriented forward substitution (once row r of the
+            // column is final, every later row's partial sum takes its term)
+            if (ok) {
+                const int b0 = 16 * gw, c = lane & 15;
+                float x[16];
+#pragma unroll
+                for (int r = 0; r < 16; ++r) x[r] = 0.0f;
 #pragma unroll
                 for (int r = 0; r < 16; ++r) {
-                    float acc = 0.0f;
+                    const float tr = (r == c) ? 1.0f : (r < c ? 0.0f : -x[r]);
+                    x[r] = tr;
 #pragma unroll
-                    for (int m = 0; m < r; ++m) acc = fmaf(Am[(b0 + r) * LD + b0 + m], tcol[m], acc);
-                    tcol[r] = (r == c) ? 1.0f : -acc;
+                    for (int r2 = r + 1; r2 < 16; ++r2) x[r2] = fmaf(Am[(b0 + r2) * LD + b0 + r], tr, x[r2]);
                 }
                 if (lane < 16) {
 #pragma unroll
-                    for (int r = 0; r < 16; ++r) Tf[(b0 + r) * LD + b0 + c] = (r < c) ? 0.0f : tcol[r];
+                    for (int r = 0; r < 16; ++r) Tf[(b0 + r) * LD + b0 + c] = x[r];
                 }
             }
-            wy_epi_bar();
-            // ---- blocks below the diagonal, one diagonal d at a time:
-            //      Y_ij = sum_{m=j}^{i-1} A_im T_mj ;  T_ij = -T_ii Y_ij
-            for (int d = 1; d < 4; ++d) {
-                const int nb = 4 - d;  // blocks on this diagonal: (j + d, j), j = 0 .. nb-1
-                const int r = et >> 4, c = et & 15;
-                if (ok) {
-                    for (int bj = 0; bj < nb; ++bj) {
-                        const int bi = bj + d;
-                        float acc = 0.0f;
-                        for (int bm = bj; bm < bi; ++bm)
-#pragma unroll
-                            for (int k = 0; k < 16; ++k)
-                                acc = fmaf(Am[(16 * bi + r) * LD + 16 * bm + k], Tf[(16 * bm + k) * LD + 16 * bj + c], acc);
-                        Yb[bj * 256 + r * 16 + c] = acc;
-                    }
-                }
-                wy_epi_bar();
-                if (ok) {
-                    for (int bj = 0; bj < nb; ++bj) {
-                        const int bi = bj + d;
-                        float acc = 0.0f;
-#pragma unroll
-                        for (int k = 0; k < 16; ++k)
-                            acc = fmaf(Tf[(16 * bi + r) * LD + 16 * bi + k], Yb[bj * 256 + k * 16 + c], acc);
-                        Tf[(16 * bi + r) * LD + 16 * bj + c] = -acc;
-                    }
-                }
-                wy_epi_bar();
-            }
-            // ---- T -> bf16 tile (128-byte swizzle, K-major A operand of the W / U products)
+            wy_group_bar(grp);
+            // ---- blocks below the diagonal: B_im = T_ii A_im for the six pairs m < i,
+            // then per diagonal d: T_ij = -sum_{m=j}^{i-1} B_im T_mj
+            // (thread: block pair of round q, row r, columns c4..c4+3)
+            const int r = (gt >> 2) & 15, c4 = 4 * (gt & 3), sub = gt >> 6;  // two blocks per round
             if (ok) {
-                uint8_t* tt = smem + Cfg::kOffT + a * 8192;
-                const int r = et >> 2, c0 = 16 * (et & 3);
 #pragma unroll
-                for (int c = 0; c < 16; c += 8) {
-                    uint4 v;
-                    const float* src = Tf + r * LD + c0 + c;
-                    v.x = pack_bf16x2(c0 + c + 0 <= r ? src[0] : 0.0f, c0 + c + 1 <= r ? src[1] : 0.0f);
-                    v.y = pack_bf16x2(c0 + c + 2 <= r ? src[2] : 0.0f, c0 + c + 3 <= r ? src[3] : 0.0f);
-                    v.z = pack_bf16x2(c0 + c + 4 <= r ? src[4] : 0.0f, c0 + c + 5 <= r ? src[5] : 0.0f);
-                    v.w = pack_bf16x2(c0 + c + 6 <= r ? src[6] : 0.0f, c0 + c + 7 <= r ? src[7] : 0.0f);
-                    *reinterpret_cast<uint4*>(tt + sw128_off(r, c0 + c, 8192)) = v;
+                for (int q = 0; q < 3; ++q) {
+                    const int pidx = 2 * q + sub;  // pairs (1,0) (2,0) (2,1) (3,0) (3,1) (3,2)
+                    const int bi = pidx == 0 ? 1 : (pidx < 3 ? 2 : 3);
+                    const int bm = pidx == 0 ? 0 : (pidx < 3 ? pidx - 1 : pidx - 3);
+                    const float4* trow = reinterpret_cast<const float4*>(Tf + (16 * bi + r) * LD + 16 * bi);
+                    float4 y = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+                    for (int k4 = 0; k4 < 4; ++k4) {
+                        const float4 t4 = trow[k4];
+                        const float tv[4] = {t4.x, t4.y, t4.z, t4.w};
+#pragma unroll
+                        for (int kk = 0; kk < 4; ++kk) {
+                            const float4 a4 =
+                                *reinterpret_cast<const float4*>(Am + (16 * bi + 4 * k4 + kk) * LD + 16 * bm + c4);
+                            y.x = fmaf(tv[kk], a4.x, y.x);
+                            y.y = fmaf(tv[kk], a4.y, y.y);
+                            y.z = fmaf(tv[kk], a4.z, y.z);
+                            y.w = fmaf(tv[kk], a4.w, y.w);
+                        }
+                    }
+                    *reinterpret_cast<float4*>(Yb + pidx * 256 + r * 16 + c4) = y;
+                }
+            }
+            wy_group_bar(grp);
+#pragma unroll
+            for (int d = 1; d < 4; ++d) {
+                if (ok) {
+                    for (int bj = sub; bj < 4 - d; bj += 2) {
+                        const int bi = bj + d;
+                        float4 y = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+                        for (int bm_off = 0; bm_off < d; ++bm_off) {
+                            const int bm = bj + bm_off;
+                            // pair index of (bi, bm): (1,0)=0 (2,0)=1 (2,1)=2 (3,0)=3 (3,1)=4 (3,2)=5
+                            const int pidx = (bi * (bi - 1)) / 2 + bm;
+                            const float* brow = Yb + pidx * 256 + r * 16;
+#pragma unroll
+                            for (int k = 0; k < 16; ++k) {
+                                const float bk = brow[k];
+                                const float4 t4 = *reinterpret_cast<const float4*>(Tf + (16 * bm + k) * LD + 16 * bj + c4);
+                                y.x = fmaf(bk, t4.x, y.x);
+                                y.y = fmaf(bk, t4.y, y.y);
+                                y.z = fmaf(bk, t4.z, y.z);
+                                y.w = fmaf(bk, t4.w, y.w);
+                            }
+                        }
+                        *reinterpret_cast<float4*>(Tf + (16 * bi + r) * LD + 16 * bj + c4) =
+                            make_float4(-y.x, -y.y, -y.z, -y.w);
+                    }
+                }
+                wy_group_bar(grp);
+            }
+            // ---- T' = bf16(T diag(beta e^g_c)), T'' = bf16(T diag(beta)) (128-byte
+            // swizzle, K-major A operands); thread: row gt/2, 32 columns
+            if (ok) {
+                uint8_t* tw = smem + Cfg::kOffT + (2 * grp) * 8192;
+                uint8_t* tu = tw + 8192;
+                const int row = gt >> 1, cb0 = 32 * (gt & 1);
+#pragma unroll
+                for (int cg8 = 0; cg8 < 4; ++cg8) {
+                    const int c0 = cb0 + 8 * cg8;
+                    uint32_t pw[4], pu[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int c = c0 + 2 * e;
+                        const float t0 = (c <= row) ? Tf[row * LD + c] : 0.0f;
+                        const float t1 = (c + 1 <= row) ? Tf[row * LD + c + 1] : 0.0f;
+                        const float b0 = sb[c], b1 = sb[c + 1];
+                        const float d0 = sd[c], d1 = sd[c + 1];
+                        pw[e] = pack_bf16x2(__fmul_rn(t0, d0), __fmul_rn(t1, d1));
+                        pu[e] = pack_bf16x2(__fmul_rn(t0, b0), __fmul_rn(t1, b1));
+                    }
+                    *reinterpret_cast<uint4*>(tw + sw128_off(row, c0, 8192)) = make_uint4(pw[0], pw[1], pw[2], pw[3]);
+                    *reinterpret_cast<uint4*>(tu + sw128_off(row, c0, 8192)) = make_uint4(pu[0], pu[1], pu[2], pu[3]);
+                }
+                if (t.len < kChunk) {
+                    // rows of k and v past the chunk's end belong to another sequence (or
+                    // are fill): zero them so that no value of theirs reaches a product
+                    const int rows = kChunk - static_cast<int>(t.len);
+                    for (int e = gt; e < (Cfg::kSubK + Cfg::kSubV) * rows * 8; e += 128) {
+                        const int tsub = e / (rows * 8), rr = static_cast<int>(t.len) + (e / 8) % rows, c8 = e & 7;
+                        uint8_t* base = tsub < Cfg::kSubK ? st + Cfg::kOffK + tsub * 8192
+                                                          : st + Cfg::kOffV + (tsub - Cfg::kSubK) * 8192;
+                        *reinterpret_cast<uint4*>(base + rr * 128 + c8 * 16) = make_uint4(0, 0, 0, 0);
+                    }
                 }
             }
             fence_proxy_async_smem();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&t_ready[a]);
-            // ---- the previous tile's w and u
-            if (it >= 1) output(it - 1, prev);
-            prev = t;
-            ++it;
+            if (lane == 0) mbar_arrive(&t_ready[grp]);
+            // ---- w, u: TMEM rows (32x32b: lane l of the warp reads lane 32 qd + l, which
+            // holds row 16 qd + l for l < 16) -> 16-byte stores
+            if (ok) ok = mbar_wait(&wu_full[grp], par, ctl, 0x40);
+            ok = __all_sync(0xffffffffu, ok) != 0;
+            if (ok) {
+                tc_fence_after();
+                const int i = 16 * qd + lane;
+                const bool live = lane < 16 && i < t.len;
+                __nv_bfloat16* wr = p.w + t.b * p.w_sb + (t.t0 + i) * p.w_st + t.hv * p.w_sh;
+                __nv_bfloat16* ur = p.u + t.b * p.u_sb + (t.t0 + i) * p.u_st + t.hv * p.u_sh;
+#pragma unroll
+                for (int c0 = 0; c0 < K_ + V_; c0 += 32) {
+                    const bool is_w = c0 < K_;
+                    const uint32_t col = is_w ? c0 : Cfg::kTmemU + (c0 - K_);
+                    uint32_t x[2][16];
+                    tmem_ld_32x32b_x16(acc + ((32u * qd) << 16) + col, x[0]);
+                    tmem_ld_32x32b_x16(acc + ((32u * qd) << 16) + col + 16, x[1]);
+                    tmem_wait_ld();
+                    if (live) {
+                        __nv_bfloat16* dst = is_w ? wr + c0 : ur + (c0 - K_);
+#pragma unroll
+                        for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+                            for (int q8 = 0; q8 < 2; ++q8) {
+                                uint4 v;
+                                v.x = pack_bf16x2(__uint_as_float(x[hh][8 * q8 + 0]), __uint_as_float(x[hh][8 * q8 + 1]));
+                                v.y = pack_bf16x2(__uint_as_float(x[hh][8 * q8 + 2]), __uint_as_float(x[hh][8 * q8 + 3]));
+                                v.z = pack_bf16x2(__uint_as_float(x[hh][8 * q8 + 4]), __uint_as_float(x[hh][8 * q8 + 5]));
+                                v.w = pack_bf16x2(__uint_as_float(x[hh][8 * q8 + 6]), __uint_as_float(x[hh][8 * q8 + 7]));
+                                *reinterpret_cast<uint4*>(dst + 16 * hh + 8 * q8) = v;
+                            }
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[grp]);
         }
-        if (it >= 1) output(it - 1, prev);
     }
 
     tc_fence_before();
