@@ -3,8 +3,10 @@ forward hidden-state recurrence of Gated DeltaNet prefill.
 
 The compute is a CUDA library with a C ABI (include/cgdr_fwd_h.h for the
 recurrence, include/cgdr_wy.h for the WY representation that feeds it,
-include/cgdr_chunk_o.h for the chunk output that consumes it); this package
-is its Python host side.  See :mod:`.api` and :mod:`.gdr`.
+include/cgdr_chunk_o.h for the chunk output that consumes it, and
+include/cgdr_gdr.h for the whole chunked Gated DeltaNet forward built from
+the three); this package is its Python host side.  See :mod:`.api` and
+:mod:`.gdr`.
 """
 
 from .api import (  # noqa: F401
@@ -16,7 +18,14 @@ from .api import (  # noqa: F401
     read_device_status,
     run,
 )
-from .gdr import ChunkGatedDeltaRuleFwdO, ChunkGatedDeltaRuleWY, chunk_fwd_o, chunk_wy_fwd  # noqa: F401
+from .gdr import (  # noqa: F401
+    ChunkGatedDeltaRule,
+    ChunkGatedDeltaRuleFwdO,
+    ChunkGatedDeltaRuleWY,
+    chunk_fwd_o,
+    chunk_gated_delta_rule,
+    chunk_wy_fwd,
+)
 from ._lib import CgdrError, CgdrValueError  # noqa: F401
 
 __all__ = [
@@ -31,6 +40,8 @@ __all__ = [
     "chunk_fwd_o",
     "ChunkGatedDeltaRuleWY",
     "chunk_wy_fwd",
+    "ChunkGatedDeltaRule",
+    "chunk_gated_delta_rule",
     "CgdrError",
     "CgdrValueError",
 ]

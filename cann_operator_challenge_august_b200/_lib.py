@@ -57,6 +57,11 @@ EXPORTS_BY_HEADER = {
         "cgdrChunkGatedDeltaRuleWY",
         "cgdrDestroyWyExecutor",
     ),
+    "cgdr_gdr.h": (
+        "cgdrChunkGatedDeltaRuleGetWorkspaceSize",
+        "cgdrChunkGatedDeltaRule",
+        "cgdrDestroyGdrExecutor",
+    ),
 }
 EXPORTS = tuple(sym for syms in EXPORTS_BY_HEADER.values() for sym in syms)
 
@@ -156,6 +161,12 @@ def load() -> ctypes.CDLL:
     lib.cgdrChunkGatedDeltaRuleWY.restype = ctypes.c_int
     lib.cgdrDestroyWyExecutor.argtypes = [ctypes.c_void_p]
     lib.cgdrDestroyWyExecutor.restype = None
+    lib.cgdrChunkGatedDeltaRuleGetWorkspaceSize.argtypes = [T] * 7 + [ctypes.c_float, T, T, u64p, exp]
+    lib.cgdrChunkGatedDeltaRuleGetWorkspaceSize.restype = ctypes.c_int
+    lib.cgdrChunkGatedDeltaRule.argtypes = [ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p, ctypes.c_void_p]
+    lib.cgdrChunkGatedDeltaRule.restype = ctypes.c_int
+    lib.cgdrDestroyGdrExecutor.argtypes = [ctypes.c_void_p]
+    lib.cgdrDestroyGdrExecutor.restype = None
     lib.cgdrGetAbiVersion.argtypes = []
     lib.cgdrGetAbiVersion.restype = ctypes.c_int32
     _lib = lib

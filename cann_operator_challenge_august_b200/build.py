@@ -18,7 +18,7 @@ from pathlib import Path
 PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 LIB = PKG / "libcgdr_fwd_h.so"
-SOURCES = [PKG / "csrc" / n for n in ("cgdr_fwd_h.cu", "cgdr_chunk_o.cu", "cgdr_wy.cu", "host_util.cu")]
+SOURCES = [PKG / "csrc" / n for n in ("cgdr_fwd_h.cu", "cgdr_chunk_o.cu", "cgdr_wy.cu", "cgdr_gdr.cu", "host_util.cu")]
 HEADERS = sorted((PKG / "csrc").glob("*.cuh")) + sorted((ROOT / "include").glob("*.h"))
 
 NVCC_FLAGS = [

@@ -8,6 +8,7 @@
 #include <new>
 
 #include "../../include/cgdr_chunk_o.h"
+#include "host_stages.cuh"
 #include "host_util.cuh"
 #include "kernel_chunk_o.cuh"
 
@@ -214,14 +215,25 @@ cgdrStatus cgdrChunkGatedDeltaRuleFwdO(void* workspace, uint64_t workspace_size,
     if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
         return fail(CGDR_STATUS_WORKSPACE_TOO_SMALL, "workspace must be 256-byte aligned");
     cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+    cudaError_t e = cudaMemsetAsync(workspace, 0, kHeader, stream);
+    if (e != cudaSuccess) return fail(CGDR_STATUS_CUDA_ERROR, "cudaMemsetAsync: %s", cudaGetErrorString(e));
+    return cgdr::host::chunk_o_enqueue(executor, static_cast<int*>(workspace), stream);
+}
+
+}  // extern "C"
+
+namespace cgdr {
+namespace host {
+
+cgdrStatus chunk_o_enqueue(const cgdrChunkOExecutor* executor, int* status, cudaStream_t stream)
+{
     ChunkOArgs args;
     memset(&args, 0, sizeof(args));
     cgdrStatus st = build_maps_o(executor, &args.maps);
     if (st) return st;
     args.p = executor->p;
-    args.p.status = static_cast<int*>(workspace);
-    cudaError_t e = cudaMemsetAsync(workspace, 0, kHeader, stream);
-    if (e != cudaSuccess) return fail(CGDR_STATUS_CUDA_ERROR, "cudaMemsetAsync: %s", cudaGetErrorString(e));
+    args.p.status = status;
+    cudaError_t e = cudaSuccess;
     if (executor->grid == 0) return CGDR_STATUS_SUCCESS;
     const ChunkOParams& p = executor->p;
     const int vt = static_cast<int>(p.V / p.n_vtiles);
@@ -233,4 +245,5 @@ cgdrStatus cgdrChunkGatedDeltaRuleFwdO(void* workspace, uint64_t workspace_size,
     return CGDR_STATUS_SUCCESS;
 }
 
-}  // extern "C"
+}  // namespace host
+}  // namespace cgdr

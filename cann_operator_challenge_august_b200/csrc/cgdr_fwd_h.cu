@@ -12,6 +12,7 @@
 
 #include "../../include/cgdr_fwd_h.h"
 #include "common.cuh"
+#include "host_stages.cuh"
 #include "host_util.cuh"
 #include "kernel_simt.cuh"
 #include "kernel_tc.cuh"
@@ -183,8 +184,12 @@ cgdrStatus build(const cgdrTensor* k, const cgdrTensor* w, const cgdrTensor* u, 
         (st = check_inner_contiguous(u, "u")) || (st = check_inner_contiguous(h, "h")))
         return st;
     if (present(v) && (st = check_inner_contiguous(v, "v"))) return st;
-    if (present(h0) && (st = check_inner_contiguous(h0, "initial_state"))) return st;
-    if (present(fin) && (st = check_inner_contiguous(fin, "final_state"))) return st;
+    // initial and final state may be [.., K, V] with any strides (a transposed
+    // [.., V, K] view included); they are read and written once per task
+    for (const cgdrTensor* t : {h0, fin})
+        if (present(t))
+            for (int i = 0; i < t->ndim; ++i)
+                if (t->strides[i] < 0) return fail(CGDR_STATUS_BAD_STRIDE, "negative stride in a state tensor");
     if (has_cu && cu->shape[0] > 1 && cu->strides[0] != 1) return fail(CGDR_STATUS_BAD_STRIDE, "cu_seqlens must be contiguous");
     if (present(co) && co->shape[0] > 1 && co->strides[0] != 1)
         return fail(CGDR_STATUS_BAD_STRIDE, "chunk_offsets must be contiguous");
@@ -220,8 +225,12 @@ cgdrStatus build(const cgdrTensor* k, const cgdrTensor* w, const cgdrTensor* u, 
         if (present(v)) { p.v_sb = v->strides[0]; p.v_st = v->strides[1]; p.v_sh = v->strides[2]; }
         p.h_sb = h->strides[0]; p.h_sc = h->strides[1]; p.h_sh = h->strides[2]; p.h_sk = h->strides[3];
     }
-    if (present(h0)) { p.h0_sn = h0->strides[0]; p.h0_sh = h0->strides[1]; p.h0_sk = h0->strides[2]; }
-    if (present(fin)) { p.f_sn = fin->strides[0]; p.f_sh = fin->strides[1]; p.f_sk = fin->strides[2]; }
+    if (present(h0)) {
+        p.h0_sn = h0->strides[0]; p.h0_sh = h0->strides[1]; p.h0_sk = h0->strides[2]; p.h0_sv = h0->strides[3];
+    }
+    if (present(fin)) {
+        p.f_sn = fin->strides[0]; p.f_sh = fin->strides[1]; p.f_sk = fin->strides[2]; p.f_sv = fin->strides[3];
+    }
     p.io_dtype = io;
     p.h0_dtype = present(h0) ? io_of(h0->dtype) : 0;
     p.f_dtype = present(fin) ? io_of(fin->dtype) : 0;
@@ -441,14 +450,31 @@ cgdrStatus cgdrChunkGatedDeltaRuleFwdH(void* workspace, uint64_t workspace_size,
     if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
         return fail(CGDR_STATUS_WORKSPACE_TOO_SMALL, "workspace must be 256-byte aligned");
     cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
-    FwdHParams p = executor->p;
     uint8_t* ws = static_cast<uint8_t*>(workspace);
-    p.status = reinterpret_cast<int*>(ws);
     cudaError_t e = cudaMemsetAsync(ws, 0, kHeaderBytes, stream);
     if (e != cudaSuccess) return fail(CGDR_STATUS_CUDA_ERROR, "cudaMemsetAsync: %s", cudaGetErrorString(e));
+    return cgdr::host::fwd_h_enqueue(executor, reinterpret_cast<int*>(ws), ws + kHeaderBytes, stream);
+}
+
+}  // extern "C"
+
+namespace cgdr {
+namespace host {
+
+uint64_t fwd_h_meta_bytes(const cgdrExecutor* ex)
+{
+    return ex->plan.workspace_bytes - kHeaderBytes;
+}
+
+cgdrStatus fwd_h_enqueue(const cgdrExecutor* executor, int* status, uint8_t* meta, cudaStream_t stream)
+{
+    const cgdrFwdHPlan& pl = executor->plan;
+    FwdHParams p = executor->p;
+    p.status = status;
+    cudaError_t e = cudaSuccess;
     if (p.varlen) {
-        int32_t* base = reinterpret_cast<int32_t*>(ws + kHeaderBytes);
-        int32_t* order = reinterpret_cast<int32_t*>(ws + kHeaderBytes + align256(4 * static_cast<uint64_t>(p.N + 1)));
+        int32_t* base = reinterpret_cast<int32_t*>(meta);
+        int32_t* order = reinterpret_cast<int32_t*>(meta + align256(4 * static_cast<uint64_t>(p.N + 1)));
         p.seq_chunk_base = base;
         p.seq_order = order;
         varlen_prep_kernel<<<1, 1024, 0, stream>>>(p.cu_seqlens, p.N, p.T, p.NT, base, order, p.status);
@@ -479,6 +505,11 @@ cgdrStatus cgdrChunkGatedDeltaRuleFwdH(void* workspace, uint64_t workspace_size,
     }
     return CGDR_STATUS_SUCCESS;
 }
+
+}  // namespace host
+}  // namespace cgdr
+
+extern "C" {
 
 cgdrStatus cgdrReadDeviceStatus(const void* workspace, uint64_t workspace_size, void* stream, int32_t* device_status)
 {

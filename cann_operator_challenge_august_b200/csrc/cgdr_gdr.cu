@@ -1,0 +1,346 @@
+// Host side of include/cgdr_gdr.h: the chunked Gated DeltaNet forward
+// operator composed of the WY, recurrence and chunk-output kernels, with the
+// reference's argument checks (ref/chunk_gated_delta_rule/op_host/
+// chunk_gated_delta_rule_tiling.cpp:375-632 and op_api/
+// aclnn_chunk_gated_delta_rule.cpp:64-96).  No device memory is allocated.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstring>
+#include <new>
+
+#include "../../include/cgdr_chunk_o.h"
+#include "../../include/cgdr_gdr.h"
+#include "../../include/cgdr_wy.h"
+#include "common.cuh"
+#include "host_stages.cuh"
+#include "host_util.cuh"
+
+using namespace cgdr;
+using namespace cgdr::host;
+
+namespace cgdr {
+
+// Sequence metadata from actualSeqLengths (one block): cu_seqlens (int64
+// [B+1]) and chunk_indices (int64 [nt_max, 2], rows of (sequence, chunk);
+// rows past the last chunk are (-1, -1) padding).  Lengths that are negative
+// or do not sum to T set status bit 0x2; every write stays inside nt_max rows.
+__global__ void __launch_bounds__(256) gdr_meta_kernel(const int32_t* asl, int64_t B, int64_t T, int64_t nt_max,
+                                                       int64_t* cu, int64_t* chunk_base, int64_t* ci, int* status)
+{
+    __shared__ int bad;
+    if (threadIdx.x == 0) {
+        int64_t run = 0, chunks = 0;
+        int b = 0;
+        cu[0] = 0;
+        chunk_base[0] = 0;
+        for (int64_t n = 0; n < B; ++n) {
+            int64_t L = asl[n];
+            if (L < 0) {
+                b = 1;
+                L = 0;
+            }
+            run += L;
+            chunks += (L + kChunk - 1) / kChunk;
+            cu[n + 1] = run;
+            chunk_base[n + 1] = chunks;
+        }
+        if (run != T || chunks > nt_max) b = 1;
+        bad = b;
+        if (b && status) atomicOr(status, 0x2);
+    }
+    __syncthreads();
+    for (int64_t n = threadIdx.x; n < B; n += blockDim.x) {
+        const int64_t c0 = chunk_base[n], c1 = chunk_base[n + 1];
+        for (int64_t r = c0; r < c1 && r < nt_max; ++r) {
+            ci[2 * r] = n;
+            ci[2 * r + 1] = r - c0;
+        }
+    }
+    const int64_t used = bad ? 0 : chunk_base[B];
+    for (int64_t r = used + threadIdx.x; r < nt_max; r += blockDim.x) {
+        ci[2 * r] = -1;
+        ci[2 * r + 1] = -1;
+    }
+}
+
+}  // namespace cgdr
+
+struct cgdrGdrExecutor {
+    uint32_t magic;
+    cgdrTensor q, k, v, beta, h0, asl, g, out, fin;
+    bool has_g;
+    float scale;
+    int64_t B, T, Nk, Nv, Dk, Dv, nt_max;
+    // workspace layout (byte offsets)
+    uint64_t off_cu, off_cb, off_ci, off_meta, off_gc, off_w, off_u, off_vn, off_h, total;
+};
+
+namespace {
+
+constexpr uint32_t kMagicGdr = 0xC6D2D0A5u;
+constexpr uint64_t kHeader = 256;
+constexpr int64_t kMaxHeads = 64;    // tiling.cpp:504-507
+constexpr int64_t kMaxHeadDim = 128; // tiling.cpp:509-512
+
+cgdrTensor view(void* data, int32_t dtype, std::initializer_list<int64_t> shape, std::initializer_list<int64_t> strides)
+{
+    cgdrTensor t;
+    memset(&t, 0, sizeof(t));
+    t.data = data;
+    t.dtype = dtype;
+    t.ndim = static_cast<int32_t>(shape.size());
+    int i = 0;
+    for (int64_t x : shape) t.shape[i++] = x;
+    i = 0;
+    for (int64_t x : strides) t.strides[i++] = x;
+    return t;
+}
+
+cgdrTensor contiguous(void* data, int32_t dtype, std::initializer_list<int64_t> shape)
+{
+    cgdrTensor t = view(data, dtype, shape, shape);
+    int64_t s = 1;
+    for (int i = t.ndim - 1; i >= 0; --i) {
+        t.strides[i] = s;
+        s *= t.shape[i];
+    }
+    return t;
+}
+
+bool has_empty(const cgdrTensor* t)
+{
+    for (int i = 0; i < t->ndim; ++i)
+        if (t->shape[i] == 0) return true;
+    return false;
+}
+
+bool sixteen(const cgdrTensor* t)
+{
+    if ((reinterpret_cast<uintptr_t>(t->data) & 15) != 0) return false;
+    for (int i = 0; i < t->ndim - 1; ++i)
+        if ((t->strides[i] * 2) % 16 != 0) return false;
+    return t->strides[t->ndim - 1] == 1;
+}
+
+cgdrStatus build_gdr(const cgdrTensor* q, const cgdrTensor* k, const cgdrTensor* v, const cgdrTensor* beta,
+                     const cgdrTensor* h0, const cgdrTensor* asl, const cgdrTensor* g, float scale,
+                     const cgdrTensor* out, const cgdrTensor* fin, uint64_t* ws_size, cgdrGdrExecutor** exo)
+{
+    if (!ws_size || !exo) return fail(CGDR_STATUS_NULL_ARGUMENT, "workspaceSize and executor must not be NULL");
+    *exo = nullptr;
+    // aclnn_chunk_gated_delta_rule.cpp:64-76: every tensor but g is required
+    if (!present(q) || !present(k) || !present(v) || !present(h0) || !present(beta) || !present(asl) ||
+        !present(out) || !present(fin))
+        return fail(CGDR_STATUS_NULL_ARGUMENT,
+                    "query, key, value, initialState, beta, actualSeqLengths, out and finalState are required");
+    const bool has_g = present(g);
+    // dtypes (aclnn_chunk_gated_delta_rule.cpp:54-95)
+    for (const cgdrTensor* t : {q, k, v, beta, out})
+        if (t->dtype != CGDR_DT_BF16) return fail(CGDR_STATUS_BAD_DTYPE, "query, key, value, beta and out must be bfloat16");
+    for (const cgdrTensor* t : {h0, fin})
+        if (t->dtype != CGDR_DT_BF16 && t->dtype != CGDR_DT_FLOAT32)
+            return fail(CGDR_STATUS_BAD_DTYPE, "initialState and finalState must be bfloat16 or float32");
+    if (asl->dtype != CGDR_DT_INT32) return fail(CGDR_STATUS_BAD_DTYPE, "actualSeqLengths must be int32");
+    if (has_g && g->dtype != CGDR_DT_FLOAT32) return fail(CGDR_STATUS_BAD_DTYPE, "g must be float32");
+    // ranks (tiling.cpp:535-541)
+    cgdrStatus st;
+    if ((st = check_rank(q, 3, "query")) || (st = check_rank(k, 3, "key")) || (st = check_rank(v, 3, "value")) ||
+        (st = check_rank(beta, 2, "beta")) || (st = check_rank(h0, 4, "initial_state")) ||
+        (st = check_rank(asl, 1, "actual_seq_lengths")) || (st = check_rank(out, 3, "out")) ||
+        (st = check_rank(fin, 4, "final_state")))
+        return st;
+    if (has_g && (st = check_rank(g, 2, "g"))) return st;
+    // dimensions (tiling.cpp:495-518)
+    const int64_t T = q->shape[0], Nk = q->shape[1], Dk = q->shape[2], Nv = v->shape[1], Dv = v->shape[2];
+    const int64_t B = h0->shape[0];
+    if (T <= 0 || B <= 0 || Nk <= 0 || Dk <= 0 || Nv <= 0 || Dv <= 0)
+        return fail(CGDR_STATUS_BAD_SHAPE,
+                    "T, B, Nk, Dk, Nv, Dv should be greater than 0, but T=%lld, B=%lld, Nk=%lld, Dk=%lld, Nv=%lld, Dv=%lld",
+                    (long long)T, (long long)B, (long long)Nk, (long long)Dk, (long long)Nv, (long long)Dv);
+    if (Nk > kMaxHeads || Nv > kMaxHeads)
+        return fail(CGDR_STATUS_BAD_SHAPE, "nk and nv should no bigger than 64, but nk is %lld, nv is %lld", (long long)Nk,
+                    (long long)Nv);
+    if (Dv > kMaxHeadDim || Dk > kMaxHeadDim)
+        return fail(CGDR_STATUS_BAD_SHAPE, "dv and dk should be no bigger than 128, but dv is %lld, dk is %lld",
+                    (long long)Dv, (long long)Dk);
+    if (Nv % Nk != 0)
+        return fail(CGDR_STATUS_BAD_SHAPE, "nv should be an integer multiple of nk, but nv is %lld, nk is %lld",
+                    (long long)Nv, (long long)Nk);
+    // expected shapes (tiling.cpp:375-490)
+    if (!shape_is(k, {T, Nk, Dk})) return fail(CGDR_STATUS_BAD_SHAPE, "The shape of key parameter is not expected");
+    if (!shape_is(v, {T, Nv, Dv})) return fail(CGDR_STATUS_BAD_SHAPE, "The shape of value parameter is not expected");
+    if (!shape_is(beta, {T, Nv})) return fail(CGDR_STATUS_BAD_SHAPE, "The shape of beta parameter is not expected");
+    if (!shape_is(h0, {B, Nv, Dv, Dk}))
+        return fail(CGDR_STATUS_BAD_SHAPE, "The shape of initial_state parameter is not expected");
+    if (!shape_is(asl, {B})) return fail(CGDR_STATUS_BAD_SHAPE, "The shape of actual_seq_lengths parameter is not expected");
+    if (!shape_is(out, {T, Nv, Dv})) return fail(CGDR_STATUS_BAD_SHAPE, "The shape of out parameter is not expected");
+    if (!shape_is(fin, {B, Nv, Dv, Dk}))
+        return fail(CGDR_STATUS_BAD_SHAPE, "The shape of final_state parameter is not expected");
+    if (has_g && !shape_is(g, {T, Nv})) return fail(CGDR_STATUS_BAD_SHAPE, "The shape of g parameter is not expected");
+    // empty tensors (tiling.cpp:567-590)
+    for (const cgdrTensor* t : {q, k, v, beta, h0, asl, out, fin})
+        if (has_empty(t)) return fail(CGDR_STATUS_BAD_SHAPE, "empty tensors are not supported");
+    // this build
+    if (!(Dk == 64 || Dk == 128) || !(Dv == 64 || Dv == 128))
+        return fail(CGDR_STATUS_UNSUPPORTED, "this build computes Dk and Dv in {64, 128}, got Dk=%lld, Dv=%lld",
+                    (long long)Dk, (long long)Dv);
+    for (const cgdrTensor* t : {q, k, v, out})
+        if (!sixteen(t))
+            return fail(CGDR_STATUS_BAD_STRIDE,
+                        "query, key, value and out need a contiguous last dimension and 16-byte aligned strides");
+    if (asl->strides[0] != 1 && B > 1) return fail(CGDR_STATUS_BAD_STRIDE, "actualSeqLengths must be contiguous");
+    if (T >= (int64_t(1) << 31)) return fail(CGDR_STATUS_UNSUPPORTED, "T must fit in 31 bits");
+
+    cgdrGdrExecutor* ex = new (std::nothrow) cgdrGdrExecutor();
+    if (!ex) return fail(CGDR_STATUS_UNSUPPORTED, "out of host memory");
+    ex->magic = kMagicGdr;
+    ex->q = *q; ex->k = *k; ex->v = *v; ex->beta = *beta; ex->h0 = *h0; ex->asl = *asl;
+    ex->out = *out; ex->fin = *fin;
+    ex->has_g = has_g;
+    if (has_g) ex->g = *g;
+    ex->scale = scale > 0.0f ? scale : static_cast<float>(1.0 / std::sqrt(static_cast<double>(Dk)));
+    ex->B = B; ex->T = T; ex->Nk = Nk; ex->Nv = Nv; ex->Dk = Dk; ex->Dv = Dv;
+    ex->nt_max = (T + kChunk - 1) / kChunk + B - 1;
+    uint64_t off = kHeader;
+    auto take = [&](uint64_t bytes) {
+        const uint64_t at = off;
+        off += align256(bytes);
+        return at;
+    };
+    ex->off_cu = take(8 * static_cast<uint64_t>(B + 1));
+    ex->off_cb = take(8 * static_cast<uint64_t>(B + 1));
+    ex->off_ci = take(16 * static_cast<uint64_t>(ex->nt_max));
+    // the recurrence's varlen metadata: chunk base [N+1] and launch order [N], int32
+    ex->off_meta = take(align256(4 * static_cast<uint64_t>(B + 1)) + align256(4 * static_cast<uint64_t>(B)));
+    ex->off_gc = take(4 * static_cast<uint64_t>(T * Nv));
+    ex->off_w = take(2 * static_cast<uint64_t>(T * Nv * Dk));
+    ex->off_u = take(2 * static_cast<uint64_t>(T * Nv * Dv));
+    ex->off_vn = take(2 * static_cast<uint64_t>(T * Nv * Dv));
+    ex->off_h = take(2 * static_cast<uint64_t>(ex->nt_max * Nv * Dk * Dv));
+    ex->total = off;
+    *ws_size = off;
+    *exo = ex;
+    g_err[0] = '\0';
+    return CGDR_STATUS_SUCCESS;
+}
+
+}  // namespace
+
+extern "C" {
+
+cgdrStatus cgdrChunkGatedDeltaRuleGetWorkspaceSize(const cgdrTensor* query, const cgdrTensor* key,
+                                                   const cgdrTensor* value, const cgdrTensor* beta,
+                                                   const cgdrTensor* initialState, const cgdrTensor* actualSeqLengths,
+                                                   const cgdrTensor* gOptional, float scaleValue,
+                                                   const cgdrTensor* out, const cgdrTensor* finalState,
+                                                   uint64_t* workspaceSize, cgdrGdrExecutor** executor)
+{
+    return build_gdr(query, key, value, beta, initialState, actualSeqLengths, gOptional, scaleValue, out, finalState,
+                     workspaceSize, executor);
+}
+
+void cgdrDestroyGdrExecutor(cgdrGdrExecutor* executor)
+{
+    if (executor && executor->magic == kMagicGdr) {
+        executor->magic = 0;
+        delete executor;
+    }
+}
+
+cgdrStatus cgdrChunkGatedDeltaRule(void* workspace, uint64_t workspaceSize, cgdrGdrExecutor* executor, void* stream_ptr)
+{
+    if (!executor || executor->magic != kMagicGdr) return fail(CGDR_STATUS_BAD_EXECUTOR, "invalid executor");
+    struct Guard {
+        cgdrGdrExecutor* e;
+        ~Guard() { cgdrDestroyGdrExecutor(e); }
+    } guard{executor};
+    const cgdrGdrExecutor& ex = *executor;
+    if (!workspace) return fail(CGDR_STATUS_NULL_ARGUMENT, "workspace must not be NULL");
+    if (workspaceSize < ex.total)
+        return fail(CGDR_STATUS_WORKSPACE_TOO_SMALL, "workspace of %llu bytes is smaller than the %llu required",
+                    (unsigned long long)workspaceSize, (unsigned long long)ex.total);
+    if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
+        return fail(CGDR_STATUS_WORKSPACE_TOO_SMALL, "workspace must be 256-byte aligned");
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    int* status = reinterpret_cast<int*>(ws);
+    const int64_t T = ex.T, Nk = ex.Nk, Nv = ex.Nv, Dk = ex.Dk, Dv = ex.Dv, B = ex.B, NT = ex.nt_max;
+
+    // views: the TND tensors as [1, T, heads, dim] (a packed varlen batch), the
+    // [B, Nv, Dv, Dk] states as [B, Nv, K=Dk, V=Dv] by their strides
+    const cgdrTensor q4 = view(ex.q.data, CGDR_DT_BF16, {1, T, Nk, Dk},
+                               {T * ex.q.strides[0], ex.q.strides[0], ex.q.strides[1], ex.q.strides[2]});
+    const cgdrTensor k4 = view(ex.k.data, CGDR_DT_BF16, {1, T, Nk, Dk},
+                               {T * ex.k.strides[0], ex.k.strides[0], ex.k.strides[1], ex.k.strides[2]});
+    const cgdrTensor v4 = view(ex.v.data, CGDR_DT_BF16, {1, T, Nv, Dv},
+                               {T * ex.v.strides[0], ex.v.strides[0], ex.v.strides[1], ex.v.strides[2]});
+    const cgdrTensor o4 = view(ex.out.data, CGDR_DT_BF16, {1, T, Nv, Dv},
+                               {T * ex.out.strides[0], ex.out.strides[0], ex.out.strides[1], ex.out.strides[2]});
+    const cgdrTensor b3 = view(ex.beta.data, CGDR_DT_BF16, {1, T, Nv},
+                               {T * ex.beta.strides[0], ex.beta.strides[0], ex.beta.strides[1]});
+    cgdrTensor g3;
+    memset(&g3, 0, sizeof(g3));
+    if (ex.has_g) g3 = view(ex.g.data, CGDR_DT_FLOAT32, {1, T, Nv}, {T * ex.g.strides[0], ex.g.strides[0], ex.g.strides[1]});
+    const cgdrTensor h0 = view(ex.h0.data, ex.h0.dtype, {B, Nv, Dk, Dv},
+                               {ex.h0.strides[0], ex.h0.strides[1], ex.h0.strides[3], ex.h0.strides[2]});
+    const cgdrTensor fin = view(ex.fin.data, ex.fin.dtype, {B, Nv, Dk, Dv},
+                                {ex.fin.strides[0], ex.fin.strides[1], ex.fin.strides[3], ex.fin.strides[2]});
+    // workspace tensors
+    const cgdrTensor cu = contiguous(ws + ex.off_cu, CGDR_DT_INT64, {B + 1});
+    const cgdrTensor ci = contiguous(ws + ex.off_ci, CGDR_DT_INT64, {NT, 2});
+    const cgdrTensor gc = contiguous(ws + ex.off_gc, CGDR_DT_FLOAT32, {1, T, Nv});
+    const cgdrTensor w = contiguous(ws + ex.off_w, CGDR_DT_BF16, {1, T, Nv, Dk});
+    const cgdrTensor u = contiguous(ws + ex.off_u, CGDR_DT_BF16, {1, T, Nv, Dv});
+    const cgdrTensor vn = contiguous(ws + ex.off_vn, CGDR_DT_BF16, {1, T, Nv, Dv});
+    const cgdrTensor h = contiguous(ws + ex.off_h, CGDR_DT_BF16, {1, NT, Nv, Dk, Dv});
+
+    // plans of the three stages (host only)
+    cgdrWyExecutor* e_wy = nullptr;
+    cgdrExecutor* e_h = nullptr;
+    cgdrChunkOExecutor* e_o = nullptr;
+    struct Owned {
+        cgdrWyExecutor*& a;
+        cgdrExecutor*& b;
+        cgdrChunkOExecutor*& c;
+        ~Owned()
+        {
+            cgdrDestroyWyExecutor(a);
+            cgdrDestroyExecutor(b);
+            cgdrDestroyChunkOExecutor(c);
+        }
+    } owned{e_wy, e_h, e_o};
+    uint64_t sz = 0;
+    cgdrStatus st;
+    if ((st = cgdrChunkGatedDeltaRuleWYGetWorkspaceSize(&k4, &v4, &b3, ex.has_g ? &g3 : nullptr, &cu, &ci, kChunk, &w, &u,
+                                                        &gc, nullptr, &sz, &e_wy)))
+        return st;
+    cgdrFwdHOptions opt;
+    memset(&opt, 0, sizeof(opt));
+    opt.layout = CGDR_LAYOUT_TOKEN_MAJOR;
+    opt.numerics = CGDR_NUMERICS_FP32_STATE;
+    if ((st = cgdrChunkGatedDeltaRuleFwdHGetWorkspaceSizeEx(&k4, &w, &u, &gc, &h0, &cu, &ci, nullptr, kChunk, &h, &vn,
+                                                            &fin, &opt, &sz, &e_h)))
+        return st;
+    if (fwd_h_meta_bytes(e_h) > align256(4 * static_cast<uint64_t>(B + 1)) + align256(4 * static_cast<uint64_t>(B)))
+        return fail(CGDR_STATUS_UNSUPPORTED, "internal: recurrence metadata does not fit");
+    if ((st = cgdrChunkGatedDeltaRuleFwdOGetWorkspaceSize(&q4, &k4, &vn, &h, &gc, &cu, &ci, ex.scale, kChunk, &o4,
+                                                          nullptr, &sz, &e_o)))
+        return st;
+
+    // enqueue: status word, metadata, WY, recurrence, chunk output (one stream)
+    cudaError_t e = cudaMemsetAsync(ws, 0, kHeader, stream);
+    if (e != cudaSuccess) return fail(CGDR_STATUS_CUDA_ERROR, "cudaMemsetAsync: %s", cudaGetErrorString(e));
+    gdr_meta_kernel<<<1, 256, 0, stream>>>(static_cast<const int32_t*>(ex.asl.data), B, T, NT,
+                                           reinterpret_cast<int64_t*>(ws + ex.off_cu),
+                                           reinterpret_cast<int64_t*>(ws + ex.off_cb),
+                                           reinterpret_cast<int64_t*>(ws + ex.off_ci), status);
+    if ((e = cudaGetLastError()) != cudaSuccess)
+        return fail(CGDR_STATUS_CUDA_ERROR, "metadata kernel launch: %s", cudaGetErrorString(e));
+    if ((st = wy_enqueue(e_wy, status, stream))) return st;
+    if ((st = fwd_h_enqueue(e_h, status, ws + ex.off_meta, stream))) return st;
+    if ((st = chunk_o_enqueue(e_o, status, stream))) return st;
+    return CGDR_STATUS_SUCCESS;
+}
+
+}  // extern "C"

@@ -7,6 +7,7 @@
 #include <new>
 
 #include "../../include/cgdr_wy.h"
+#include "host_stages.cuh"
 #include "host_util.cuh"
 #include "kernel_wy.cuh"
 
@@ -192,6 +193,18 @@ cgdrStatus cgdrChunkGatedDeltaRuleWY(void* workspace, uint64_t workspace_size, c
     if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
         return fail(CGDR_STATUS_WORKSPACE_TOO_SMALL, "workspace must be 256-byte aligned");
     cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+    cudaError_t e = cudaMemsetAsync(workspace, 0, kHeader, stream);
+    if (e != cudaSuccess) return fail(CGDR_STATUS_CUDA_ERROR, "cudaMemsetAsync: %s", cudaGetErrorString(e));
+    return cgdr::host::wy_enqueue(executor, static_cast<int*>(workspace), stream);
+}
+
+}  // extern "C"
+
+namespace cgdr {
+namespace host {
+
+cgdrStatus wy_enqueue(const cgdrWyExecutor* executor, int* status, cudaStream_t stream)
+{
     WyArgs args;
     memset(&args, 0, sizeof(args));
     const WyParams& p = executor->p;
@@ -209,9 +222,8 @@ cgdrStatus cgdrChunkGatedDeltaRuleWY(void* workspace, uint64_t workspace_size, c
         if ((st = make_map(&args.maps.v, t.data, 4, size, stride, box, "v"))) return st;
     }
     args.p = p;
-    args.p.status = static_cast<int*>(workspace);
-    cudaError_t e = cudaMemsetAsync(workspace, 0, kHeader, stream);
-    if (e != cudaSuccess) return fail(CGDR_STATUS_CUDA_ERROR, "cudaMemsetAsync: %s", cudaGetErrorString(e));
+    args.p.status = status;
+    cudaError_t e = cudaSuccess;
     if (executor->grid == 0) return CGDR_STATUS_SUCCESS;
     if (p.K == 128)
         e = p.V == 128 ? launch_wy<128, 128>(args, executor->grid, stream) : launch_wy<128, 64>(args, executor->grid, stream);
@@ -221,4 +233,5 @@ cgdrStatus cgdrChunkGatedDeltaRuleWY(void* workspace, uint64_t workspace_size, c
     return CGDR_STATUS_SUCCESS;
 }
 
-}  // extern "C"
+}  // namespace host
+}  // namespace cgdr

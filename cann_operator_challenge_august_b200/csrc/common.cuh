@@ -38,8 +38,8 @@ struct FwdHParams {
     int64_t g_sb, g_st, g_sh;
     int64_t v_sb, v_st, v_sh;
     int64_t h_sb, h_sc, h_sh, h_sk;
-    int64_t h0_sn, h0_sh, h0_sk;
-    int64_t f_sn, f_sh, f_sk;
+    int64_t h0_sn, h0_sh, h0_sk, h0_sv;  // h0_sv: 1, or K for a [.., V, K] (transposed) state
+    int64_t f_sn, f_sh, f_sk, f_sv;
 
     int32_t io_dtype;     // IoType of k, w, u, h, v_new
     int32_t h0_dtype;     // IoType of initial_state

@@ -114,6 +114,7 @@ struct ChunkOTile {
     int64_t b, t0, len, hrow, hv, kh;
     int v0;
     bool ok;
+    bool pad;  // chunk_indices row (-1, -1): a padding row, skipped without a flag
 };
 
 __device__ __forceinline__ ChunkOTile chunk_o_tile(const ChunkOParams& p, int64_t tile, int vt_width)
@@ -126,9 +127,11 @@ __device__ __forceinline__ ChunkOTile chunk_o_tile(const ChunkOParams& p, int64_
     t.kh = t.hv / (p.H / p.HK);
     t.v0 = vt * vt_width;
     t.ok = true;
+    t.pad = false;
     if (p.varlen) {
         const int64_t n = p.chunk_indices[2 * row];
         const int64_t c = p.chunk_indices[2 * row + 1];
+        t.pad = n == -1 && c == -1;
         t.ok = n >= 0 && n < p.N && c >= 0;
         int64_t bos = 0, eos = 0;
         if (t.ok) {
@@ -216,7 +219,7 @@ __global__ void __launch_bounds__(320, 1) chunk_o_tc_kernel(const __grid_constan
         for (int64_t tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x) {
             const ChunkOTile t = chunk_o_tile(p, tile, VT);
             if (!t.ok) {
-                if (lane == 0 && p.status) atomicOr(p.status, 0x2);
+                if (lane == 0 && p.status && !t.pad) atomicOr(p.status, 0x2);
                 continue;
             }
             const int s = static_cast<int>(it % STAGES);

@@ -59,7 +59,7 @@ __global__ void __launch_bounds__(kSimtThreads) fwd_h_simt_kernel(const __grid_c
     for (int i = tid; i < K * VT; i += kSimtThreads) {
         const int r = i / VT, c = i % VT;
         float x = 0.0f;
-        if (p.h0 && c < vcount) x = load_io(p.h0, p.h0_dtype, n * p.h0_sn + hv * p.h0_sh + r * p.h0_sk + v0 + c);
+        if (p.h0 && c < vcount) x = load_io(p.h0, p.h0_dtype, n * p.h0_sn + hv * p.h0_sh + r * p.h0_sk + (v0 + c) * p.h0_sv);
         S[i] = ref ? round_bf16(x) : x;
     }
     const int64_t nchunks = (si.len + kChunk - 1) / kChunk;
@@ -171,7 +171,7 @@ __global__ void __launch_bounds__(kSimtThreads) fwd_h_simt_kernel(const __grid_c
     if (p.final_state) {
         for (int i = tid; i < K * VT; i += kSimtThreads) {
             const int r = i / VT, cc = i % VT;
-            if (cc < vcount) store_io(p.final_state, p.f_dtype, n * p.f_sn + hv * p.f_sh + r * p.f_sk + v0 + cc, S[i]);
+            if (cc < vcount) store_io(p.final_state, p.f_dtype, n * p.f_sn + hv * p.f_sh + r * p.f_sk + (v0 + cc) * p.f_sv, S[i]);
         }
     }
 }
@@ -205,7 +205,8 @@ __global__ void __launch_bounds__(1024) varlen_prep_kernel(const int64_t* cu, in
             s_part[i] = run;
             run += v;
         }
-        if (cu[0] != 0 || cu[N] != T || run != NT) s_bad = 1;
+        // h must have a slot for every chunk (a caller may size it for more)
+        if (cu[0] != 0 || cu[N] != T || run > NT) s_bad = 1;
     }
     __syncthreads();
     long long run = s_part[tid];

@@ -303,7 +303,7 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
             st_row_col(i, row, col);
             float x = 0.0f;
             if (p.h0)
-                x = load_io(p.h0, p.h0_dtype, si.n * p.h0_sn + hv * p.h0_sh + row * p.h0_sk + v0 + col);
+                x = load_io(p.h0, p.h0_dtype, si.n * p.h0_sn + hv * p.h0_sh + row * p.h0_sk + (v0 + col) * p.h0_sv);
             st[i] = ref ? round_bf16(x) : x;
         }
         auto write_state_tile = [&]() {
@@ -603,7 +603,7 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
             for (int i = 0; i < kNState; ++i) {
                 int row, col;
                 st_row_col(i, row, col);
-                store_io(p.final_state, p.f_dtype, si.n * p.f_sn + hv * p.f_sh + row * p.f_sk + v0 + col, st[i]);
+                store_io(p.final_state, p.f_dtype, si.n * p.f_sn + hv * p.f_sh + row * p.f_sk + (v0 + col) * p.f_sv, st[i]);
             }
         }
         if (lane == 0) bulk_wait_group0();

@@ -118,6 +118,7 @@ struct WyConfig {
 struct WyTile {
     int64_t b, t0, len, hv, kh;
     bool ok;
+    bool pad;  // chunk_indices row (-1, -1): a padding row, skipped without a flag
 };
 
 __device__ __forceinline__ WyTile wy_tile(const WyParams& p, int64_t tile)
@@ -127,9 +128,11 @@ __device__ __forceinline__ WyTile wy_tile(const WyParams& p, int64_t tile)
     const int64_t row = tile / p.H;
     t.kh = t.hv / (p.H / p.HK);
     t.ok = true;
+    t.pad = false;
     if (p.varlen) {
         const int64_t n = p.chunk_indices[2 * row];
         const int64_t c = p.chunk_indices[2 * row + 1];
+        t.pad = n == -1 && c == -1;
         t.ok = n >= 0 && n < p.N && c >= 0;
         int64_t bos = 0, eos = 0;
         if (t.ok) {
@@ -211,7 +214,7 @@ __global__ void __launch_bounds__(352, 1) wy_tc_kernel(const __grid_constant__ W
             for (int64_t tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x) {
                 const WyTile t = wy_tile(p, tile);
                 if (!t.ok) {
-                    if (p.status) atomicOr(p.status, 0x2);
+                    if (p.status && !t.pad) atomicOr(p.status, 0x2);
                     continue;
                 }
                 const int s = static_cast<int>(it % STAGES);

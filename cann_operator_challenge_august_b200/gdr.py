@@ -10,6 +10,12 @@ the C ABI in include/cgdr_chunk_o.h and include/cgdr_wy.h.
   cumulative gate from k, v, beta and the per-token gate (the reference's
   stage 1, ref/chunk_gated_delta_rule/tests/pytest/
   chunk_gated_delta_rule_benchmark.py:55-83).
+* :class:`ChunkGatedDeltaRule` / :func:`chunk_gated_delta_rule` -- the whole
+  chunked Gated DeltaNet forward (WY, recurrence, chunk output) with the
+  arguments of the reference's operator: aclnnChunkGatedDeltaRule
+  (ref/chunk_gated_delta_rule/op_host/op_api/aclnn_chunk_gated_delta_rule.cpp:125)
+  and its torch_npu form npu_chunk_gated_delta_rule (argument order of
+  ref/chunk_gated_delta_rule/tests/assets/impl/golden.py:88-94).
 
 The chunk output is the consumer of ``chunk_gated_delta_rule_fwd_h``'s ``h``
 and ``v_new``: per 64-token chunk, ``o = q' h[c] + P v_new`` with
@@ -174,3 +180,75 @@ def chunk_wy_fwd(
         if status:
             raise RuntimeError(f"device status 0x{status:x}")
     return w, u, g_cum
+
+
+class ChunkGatedDeltaRule:
+    """Two-phase call of the whole operator, the aclnnChunkGatedDeltaRule
+    pattern: ``op = ChunkGatedDeltaRule(query, key, value, beta,
+    initial_state, actual_seq_lengths, g, scale, out, final_state)``
+    validates (the reference's checks) and sizes the workspace;
+    ``op(workspace)`` enqueues the metadata, WY, recurrence and chunk-output
+    kernels on the current stream."""
+
+    def __init__(self, query, key, value, beta, initial_state, actual_seq_lengths, g, scale, out, final_state):
+        lib = _lib.load()
+        self._keep = (query, key, value, beta, initial_state, actual_seq_lengths, g, out, final_state)
+        ws = ctypes.c_uint64(0)
+        ex = ctypes.c_void_p(None)
+        descs = [_desc(x) for x in (query, key, value, beta, initial_state, actual_seq_lengths, g)]
+        st = lib.cgdrChunkGatedDeltaRuleGetWorkspaceSize(
+            *[ctypes.byref(d) for d in descs], float(scale if scale is not None else 0.0), ctypes.byref(_desc(out)),
+            ctypes.byref(_desc(final_state)), ctypes.byref(ws), ctypes.byref(ex))
+        _lib.check(st, "cgdrChunkGatedDeltaRuleGetWorkspaceSize")
+        self._ex = ex
+        self.workspace_size = int(ws.value)
+
+    def __call__(self, workspace: torch.Tensor, stream: int | None = None) -> None:
+        if self._ex is None:
+            raise RuntimeError("executor already consumed")
+        ex, self._ex = self._ex, None
+        if stream is None:
+            stream = _stream_handle(workspace.device)
+        st = _lib.load().cgdrChunkGatedDeltaRule(
+            ctypes.c_void_p(workspace.data_ptr()), workspace.numel() * workspace.element_size(), ex,
+            ctypes.c_void_p(stream))
+        _lib.check(st, "cgdrChunkGatedDeltaRule")
+
+    def __del__(self):
+        if getattr(self, "_ex", None) is not None and _lib._lib is not None:
+            _lib._lib.cgdrDestroyGdrExecutor(self._ex)
+            self._ex = None
+
+
+def chunk_gated_delta_rule(
+    query: torch.Tensor,
+    key: torch.Tensor,
+    value: torch.Tensor,
+    beta: torch.Tensor,
+    initial_state: torch.Tensor,
+    actual_seq_lengths: torch.Tensor,
+    scale: float | None = None,
+    g: torch.Tensor | None = None,
+    *,
+    workspace: torch.Tensor | None = None,
+    check_device_status: bool = False,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """The reference operator's Python form (torch_npu.npu_chunk_gated_delta_rule):
+    query, key ``[T, Nk, Dk]``, value ``[T, Nv, Dv]``, beta ``[T, Nv]`` (bf16),
+    initial_state ``[B, Nv, Dv, Dk]`` (bf16 or fp32), actual_seq_lengths
+    ``[B]`` int32 (summing to T), scale (default ``Dk ** -0.5``), g ``[T, Nv]``
+    fp32 per-token log gate (optional).  Returns ``out [T, Nv, Dv]`` (bf16)
+    and ``final_state`` (the dtype of initial_state).  ``workspace`` may be a
+    caller-owned uint8 buffer of at least the planned size."""
+    _require_cuda(query, key, value, beta, initial_state, actual_seq_lengths, g)
+    out = torch.empty_like(value)
+    final_state = torch.empty_like(initial_state)
+    op = ChunkGatedDeltaRule(query, key, value, beta, initial_state, actual_seq_lengths, g, scale, out, final_state)
+    if workspace is None or workspace.numel() * workspace.element_size() < op.workspace_size:
+        workspace = torch.empty(max(op.workspace_size, 256), dtype=torch.uint8, device=value.device)
+    op(workspace)
+    if check_device_status:
+        status = read_device_status(workspace)
+        if status:
+            raise RuntimeError(f"device status 0x{status:x}")
+    return out, final_state
