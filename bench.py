@@ -362,9 +362,9 @@ def main() -> int:
     ap.add_argument("--v-tile", type=int, default=0)
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--op", choices=["fwd_h", "chunk_o", "wy"], default="fwd_h",
+    ap.add_argument("--op", choices=["fwd_h", "chunk_o", "wy", "gdr"], default="fwd_h",
                     help="fwd_h: the recurrence (the headline); chunk_o: the chunk output that consumes it; "
-                         "wy: the WY representation that feeds it")
+                         "wy: the WY representation that feeds it; gdr: the whole forward operator")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -373,6 +373,8 @@ def main() -> int:
         return main_chunk_o(args)
     if args.op == "wy" and args.impl == "ours":
         return main_stage(args)
+    if args.op == "gdr" and args.impl == "ours":
+        return main_gdr(args)
 
     if args.impl == "reference":
         world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -809,6 +811,158 @@ def main_stage(args) -> int:
                          else "fallback",
                          "algorithmic_bytes_per_launch": nbytes, "launch_ms": per_launch_ms,
                          "traffic": load_traffic(args.config, "wy"), "kernel": "wy"},
+            "clocks": clk,
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": e2e_ms},
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    return 0
+
+
+def gdr_bytes(c):
+    """Operator-level bytes of one chunked Gated DeltaNet forward: query, key,
+    value, beta, g and the initial state read once; out and the final state
+    written once (a fully fused kernel's traffic)."""
+    B, T, H, HK, K, V = c["B"], c["T"], c["H"], c["HK"], c["K"], c["V"]
+    tot = B * T
+    return tot * (2 * HK * K * 2 + H * V * 2 + H * 2 + H * 4 + H * V * 2) + 2 * B * H * K * V * 4
+
+
+def main_gdr(args) -> int:
+    """--op gdr: the whole chunked Gated DeltaNet forward (WY, recurrence,
+    chunk output) through the reference operator's call, on B sequences of T
+    tokens packed as one TND batch (actual_seq_lengths = [T] * B)."""
+    import torch
+    import cann_operator_challenge_august_b200 as cg
+
+    world, rank, local = dist_setup()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    c = shard(CONFIGS[args.config], world, rank)
+    if "seqs" in c or c["K"] > 128 or c["V"] > 128:
+        raise SystemExit("--op gdr runs the fixed-length configurations with K, V <= 128")
+    B, T, H, HK, K, V = c["B"], c["T"], c["H"], c["HK"], c["K"], c["V"]
+    g0 = torch.Generator(device=dev).manual_seed(4000 + rank)
+    tot = B * T
+    q = torch.nn.functional.normalize(torch.randn(tot, HK, K, device=dev, generator=g0), dim=-1).to(torch.bfloat16)
+    k = torch.nn.functional.normalize(torch.randn(tot, HK, K, device=dev, generator=g0), dim=-1).to(torch.bfloat16)
+    v = torch.randn(tot, H, V, device=dev, generator=g0).to(torch.bfloat16)
+    beta = torch.rand(tot, H, device=dev, generator=g0).clamp(1e-6, 1 - 1e-6).to(torch.bfloat16)
+    g = -torch.rand(tot, H, device=dev, generator=g0)
+    h0 = 0.1 * torch.randn(B, H, V, K, device=dev, generator=g0)
+    asl = torch.full((B,), T, dtype=torch.int32, device=dev)
+    out = torch.empty_like(v)
+    fin = torch.empty_like(h0)
+    op0 = cg.ChunkGatedDeltaRule(q, k, v, beta, h0, asl, g, None, out, fin)
+    ws = torch.empty(op0.workspace_size, dtype=torch.uint8, device=dev)
+    del op0
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        cg.ChunkGatedDeltaRule(q, k, v, beta, h0, asl, g, None, out, fin)(ws)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    uuid = None
+    try:
+        uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:
+        pass
+    clocks = ClockSampler(uuid)
+    clocks.start()
+    time.sleep(0.3)
+    barrier(world)
+    torch.cuda.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * args.steps)]
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_stop = torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for i in range(args.steps):
+        ev[2 * i].record(stream)
+        step()
+        ev[2 * i + 1].record(stream)
+    t_stop.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    clk = clocks.stop()
+    elapsed_ms = max_over_ranks(t_start.elapsed_time(t_stop), world)
+    per_launch_ms = max_over_ranks(sum(ev[2 * i].elapsed_time(ev[2 * i + 1]) for i in range(args.steps)) / args.steps,
+                                   world)
+    ms_per_step = elapsed_ms / args.steps
+    tokens_per_step = tot * world
+    value = tokens_per_step / (ms_per_step / 1000.0)
+
+    host = [t.cpu().pin_memory() for t in (q, k, v, beta, h0, asl, g)]
+    h2d = sum(t.numel() * t.element_size() for t in host)
+    host_out = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in (out, fin)]
+    d2h = sum(t.numel() * t.element_size() for t in host_out)
+
+    def e2e_step():
+        d = [t.to(dev, non_blocking=True) for t in host]
+        o, f = cg.chunk_gated_delta_rule(d[0], d[1], d[2], d[3], d[4], d[5], None, d[6], workspace=ws)
+        host_out[0].copy_(o, non_blocking=True)
+        host_out[1].copy_(f, non_blocking=True)
+
+    e2e_ms = e2e_value = None
+    if args.e2e_steps > 0:
+        e2e_step()
+        torch.cuda.synchronize()
+        barrier(world)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.e2e_steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = max_over_ranks(e0.elapsed_time(e1), world) / args.e2e_steps
+        e2e_value = tokens_per_step / (e2e_ms / 1000.0)
+
+    nbytes = gdr_bytes(c)
+    peak, peak_kind = load_peaks()
+    achieved = nbytes / (per_launch_ms / 1000.0) / 1e9
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import gdr_stages as G
+        f = lambda t, n: t[:n].float().cpu().numpy()  # noqa: E731
+        n1 = 64
+        t0 = time.perf_counter()
+        G.benchmark_op(f(q, n1), f(k, n1), f(v, n1), f(beta, n1), K ** -0.5, h0[:1].float().cpu().numpy(), [n1],
+                       f(g, n1))
+        t1 = time.perf_counter() - t0
+        n = int(max(64, min(T, 64 * (10.0 / max(t1, 1e-4)) // 64 * 1)))
+        n = min(T, max(64, (n // 64) * 64))
+        t0 = time.perf_counter()
+        G.benchmark_op(f(q, n), f(k, n), f(v, n), f(beta, n), K ** -0.5, h0[:1].float().cpu().numpy(), [n], f(g, n))
+        dt = time.perf_counter() - t0
+        rate = n / dt
+        threads = int(os.environ.get("OMP_NUM_THREADS", "0") or 0) or len(os.sched_getaffinity(0))
+        cpu = {"value": rate, "unit": "tokens/s", "cores": threads, "kind": "port",
+               "sample": f"the restated reference bf16 operator on the first {n} tokens of sequence 0, all {H} heads "
+                         f"({dt:.2f} s), as tokens/s"}
+    if rank == 0:
+        line = {
+            "metric": "gdr tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+            "scaling": c["scaling"], "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded, generated on device per rank, the reference operator's input ranges)",
+            "config": dict(config_block(args.config, c, world, nbytes),
+                           workload=f"{args.config}: chunked Gated DeltaNet forward (WY, recurrence, chunk output) bf16, "
+                                    f"{B} sequences of T={T} packed as TND, Nk={HK} Nv={H} Dk={K} Dv={V}, "
+                                    f"fp32 initial/final state"),
+            "gpu_launches": 4 * args.steps,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                         else "fallback",
+                         "algorithmic_bytes_per_launch": nbytes, "launch_ms": per_launch_ms,
+                         "bytes_basis": "operator inputs and outputs only (the intermediates of the three kernels "
+                                        "are not counted)",
+                         "traffic": None, "kernel": "wy+fwd_h+chunk_o"},
             "clocks": clk,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": e2e_ms},
