@@ -151,6 +151,31 @@ __device__ __forceinline__ WyTile wy_tile(const WyParams& p, int64_t tile)
     return t;
 }
 
+// 4 x 4 transpose of 32-bit values across the lanes of a quad: lane i's a[j]
+// becomes lane j's a[i] (two butterfly rounds, four shuffles).
+__device__ __forceinline__ void quad_transpose(uint32_t (&a)[4], int lane)
+{
+    const bool o1 = lane & 1, o2 = lane & 2;
+    uint32_t r0 = __shfl_xor_sync(0xffffffffu, o1 ? a[0] : a[1], 1);
+    uint32_t r1 = __shfl_xor_sync(0xffffffffu, o1 ? a[2] : a[3], 1);
+    if (o1) {
+        a[0] = r0;
+        a[2] = r1;
+    } else {
+        a[1] = r0;
+        a[3] = r1;
+    }
+    r0 = __shfl_xor_sync(0xffffffffu, o2 ? a[0] : a[2], 2);
+    r1 = __shfl_xor_sync(0xffffffffu, o2 ? a[1] : a[3], 2);
+    if (o2) {
+        a[0] = r0;
+        a[1] = r1;
+    } else {
+        a[2] = r0;
+        a[3] = r1;
+    }
+}
+
 // named barrier of epilogue group g (ids 1 and 2, 128 threads each)
 __device__ __forceinline__ void wy_group_bar(int g) { asm volatile("bar.sync %0, 128;" ::"r"(1 + g) : "memory"); }
 
@@ -435,22 +460,24 @@ __global__ void __launch_bounds__(352, 1) wy_tc_kernel(const __grid_constant__ W
                     const int bi = pidx == 0 ? 1 : (pidx < 3 ? 2 : 3);
                     const int bm = pidx == 0 ? 0 : (pidx < 3 ? pidx - 1 : pidx - 3);
                     const float4* trow = reinterpret_cast<const float4*>(Tf + (16 * bi + r) * LD + 16 * bi);
-                    float4 y = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    float4 t4[4];
 #pragma unroll
-                    for (int k4 = 0; k4 < 4; ++k4) {
-                        const float4 t4 = trow[k4];
-                        const float tv[4] = {t4.x, t4.y, t4.z, t4.w};
+                    for (int k4 = 0; k4 < 4; ++k4) t4[k4] = trow[k4];
+                    // two partial sums (k < 8, k >= 8) halve the dependency chains
+                    float4 y[2] = {make_float4(0.0f, 0.0f, 0.0f, 0.0f), make_float4(0.0f, 0.0f, 0.0f, 0.0f)};
 #pragma unroll
-                        for (int kk = 0; kk < 4; ++kk) {
-                            const float4 a4 =
-                                *reinterpret_cast<const float4*>(Am + (16 * bi + 4 * k4 + kk) * LD + 16 * bm + c4);
-                            y.x = fmaf(tv[kk], a4.x, y.x);
-                            y.y = fmaf(tv[kk], a4.y, y.y);
-                            y.z = fmaf(tv[kk], a4.z, y.z);
-                            y.w = fmaf(tv[kk], a4.w, y.w);
-                        }
+                    for (int k = 0; k < 16; ++k) {
+                        const float tk = k % 4 == 0 ? t4[k / 4].x : k % 4 == 1 ? t4[k / 4].y : k % 4 == 2 ? t4[k / 4].z
+                                                                                                          : t4[k / 4].w;
+                        const float4 a4 = *reinterpret_cast<const float4*>(Am + (16 * bi + k) * LD + 16 * bm + c4);
+                        float4& acc_ = y[k >> 3];
+                        acc_.x = fmaf(tk, a4.x, acc_.x);
+                        acc_.y = fmaf(tk, a4.y, acc_.y);
+                        acc_.z = fmaf(tk, a4.z, acc_.z);
+                        acc_.w = fmaf(tk, a4.w, acc_.w);
                     }
-                    *reinterpret_cast<float4*>(Yb + pidx * 256 + r * 16 + c4) = y;
+                    *reinterpret_cast<float4*>(Yb + pidx * 256 + r * 16 + c4) =
+                        make_float4(y[0].x + y[1].x, y[0].y + y[1].y, y[0].z + y[1].z, y[0].w + y[1].w);
                 }
             }
             wy_group_bar(grp);
@@ -521,37 +548,44 @@ __global__ void __launch_bounds__(352, 1) wy_tc_kernel(const __grid_constant__ W
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&t_ready[grp]);
-            // ---- w, u: TMEM rows (32x32b: lane l of the warp reads lane 32 qd + l, which
-            // holds row 16 qd + l for l < 16) -> 16-byte stores
+            // ---- w, u: 16x256b fragments (thread: rows ra, rb; column pairs 2(lane%4) of
+            // each 8-column group) in two batches (w, then u), a quad transpose turns the
+            // pairs into 16-byte chunks (lane l%4 takes the group l%4 of every 32 columns)
             if (ok) ok = mbar_wait(&wu_full[grp], par, ctl, 0x40);
             ok = __all_sync(0xffffffffu, ok) != 0;
             if (ok) {
                 tc_fence_after();
-                const int i = 16 * qd + lane;
-                const bool live = lane < 16 && i < t.len;
-                __nv_bfloat16* wr = p.w + t.b * p.w_sb + (t.t0 + i) * p.w_st + t.hv * p.w_sh;
-                __nv_bfloat16* ur = p.u + t.b * p.u_sb + (t.t0 + i) * p.u_st + t.hv * p.u_sh;
+                const int qi = lane & 3;
+                const bool live_a = ra < t.len, live_b = rb < t.len;
 #pragma unroll
-                for (int c0 = 0; c0 < K_ + V_; c0 += 32) {
-                    const bool is_w = c0 < K_;
-                    const uint32_t col = is_w ? c0 : Cfg::kTmemU + (c0 - K_);
-                    uint32_t x[2][16];
-                    tmem_ld_32x32b_x16(acc + ((32u * qd) << 16) + col, x[0]);
-                    tmem_ld_32x32b_x16(acc + ((32u * qd) << 16) + col + 16, x[1]);
+                for (int batch = 0; batch < 2; ++batch) {
+                    constexpr int kMaxBlk = 4;
+                    const int ncols = batch == 0 ? K_ : V_;
+                    const uint32_t col0 = batch == 0 ? 0u : Cfg::kTmemU;
+                    uint32_t x[kMaxBlk][16];
+#pragma unroll
+                    for (int cb = 0; cb < kMaxBlk; ++cb)
+                        if (cb * 32 < ncols) tmem_ld_16x256b_x4(acc + ((32u * qd) << 16) + col0 + 32 * cb, x[cb]);
                     tmem_wait_ld();
-                    if (live) {
-                        __nv_bfloat16* dst = is_w ? wr + c0 : ur + (c0 - K_);
+                    __nv_bfloat16* base = batch == 0 ? p.w + t.b * p.w_sb + t.t0 * p.w_st + t.hv * p.w_sh
+                                                     : p.u + t.b * p.u_sb + t.t0 * p.u_st + t.hv * p.u_sh;
+                    const int64_t rs = batch == 0 ? p.w_st : p.u_st;
 #pragma unroll
-                        for (int hh = 0; hh < 2; ++hh)
+                    for (int cb = 0; cb < kMaxBlk; ++cb) {
+                        if (cb * 32 >= ncols) continue;
 #pragma unroll
-                            for (int q8 = 0; q8 < 2; ++q8) {
-                                uint4 v;
-                                v.x = pack_bf16x2(__uint_as_float(x[hh][8 * q8 + 0]), __uint_as_float(x[hh][8 * q8 + 1]));
-                                v.y = pack_bf16x2(__uint_as_float(x[hh][8 * q8 + 2]), __uint_as_float(x[hh][8 * q8 + 3]));
-                                v.z = pack_bf16x2(__uint_as_float(x[hh][8 * q8 + 4]), __uint_as_float(x[hh][8 * q8 + 5]));
-                                v.w = pack_bf16x2(__uint_as_float(x[hh][8 * q8 + 6]), __uint_as_float(x[hh][8 * q8 + 7]));
-                                *reinterpret_cast<uint4*>(dst + 16 * hh + 8 * q8) = v;
-                            }
+                        for (int half = 0; half < 2; ++half) {
+                            uint32_t q4[4];
+#pragma unroll
+                            for (int jj = 0; jj < 4; ++jj)
+                                q4[jj] = pack_bf16x2(__uint_as_float(x[cb][4 * jj + 2 * half]),
+                                                     __uint_as_float(x[cb][4 * jj + 2 * half + 1]));
+                            quad_transpose(q4, lane);
+                            const int row = half ? rb : ra;
+                            if (half ? live_b : live_a)
+                                *reinterpret_cast<uint4*>(base + row * rs + 32 * cb + 8 * qi) =
+                                    make_uint4(q4[0], q4[1], q4[2], q4[3]);
+                        }
                     }
                 }
             }
