@@ -12,6 +12,7 @@ the three); this package is its Python host side.  See :mod:`.api` and
 from .api import (  # noqa: F401
     CHUNK_SIZE,
     ChunkGatedDeltaRuleFwdH,
+    chunk_capacity,
     chunk_gated_delta_rule_fwd_h,
     prepare_chunk_indices,
     prepare_chunk_offsets,
@@ -31,6 +32,7 @@ from ._lib import CgdrError, CgdrValueError  # noqa: F401
 __all__ = [
     "CHUNK_SIZE",
     "ChunkGatedDeltaRuleFwdH",
+    "chunk_capacity",
     "chunk_gated_delta_rule_fwd_h",
     "prepare_chunk_indices",
     "prepare_chunk_offsets",

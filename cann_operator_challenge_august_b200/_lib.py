@@ -57,6 +57,7 @@ EXPORTS_BY_HEADER = {
         "cgdrChunkGatedDeltaRuleWY",
         "cgdrDestroyWyExecutor",
     ),
+    "cgdr_varlen.h": ("cgdrPrepareChunkIndices",),
     "cgdr_gdr.h": (
         "cgdrChunkGatedDeltaRuleGetWorkspaceSize",
         "cgdrChunkGatedDeltaRule",
@@ -167,6 +168,8 @@ def load() -> ctypes.CDLL:
     lib.cgdrChunkGatedDeltaRule.restype = ctypes.c_int
     lib.cgdrDestroyGdrExecutor.argtypes = [ctypes.c_void_p]
     lib.cgdrDestroyGdrExecutor.restype = None
+    lib.cgdrPrepareChunkIndices.argtypes = [T, ctypes.c_int64, T, T, ctypes.c_void_p]
+    lib.cgdrPrepareChunkIndices.restype = ctypes.c_int
     lib.cgdrGetAbiVersion.argtypes = []
     lib.cgdrGetAbiVersion.restype = ctypes.c_int32
     _lib = lib

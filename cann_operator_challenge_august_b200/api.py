@@ -44,15 +44,37 @@ def _stream_handle(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
-def prepare_chunk_indices(cu_seqlens: torch.Tensor, chunk_size: int = CHUNK_SIZE) -> torch.Tensor:
+def prepare_chunk_indices(cu_seqlens: torch.Tensor, chunk_size: int = CHUNK_SIZE,
+                          capacity: int | None = None) -> torch.Tensor:
     """Rows of (sequence, chunk within the sequence) -- docs/problem.txt:251-260.
 
-    Computed on the host from the sequence lengths (one device->host copy of
-    ``cu_seqlens``) and returned on ``cu_seqlens.device``."""
+    Without ``capacity`` the list is computed on the host from the sequence
+    lengths (one device->host copy of ``cu_seqlens``, the reference's way)
+    and has exactly one row per chunk.  With ``capacity`` (at least
+    ``ceil(T / chunk_size) + N - 1``) a device kernel fills ``capacity`` rows
+    on the current stream, padding with (-1, -1) rows that the kernels skip:
+    no host synchronisation (see :func:`chunk_capacity`)."""
+    if capacity is not None:
+        if not cu_seqlens.is_cuda:
+            raise ValueError("the device chunk list needs cu_seqlens on a CUDA device")
+        out = torch.empty(int(capacity), 2, dtype=torch.int64, device=cu_seqlens.device)
+        cu = cu_seqlens.to(torch.int64).contiguous()
+        st = _lib.load().cgdrPrepareChunkIndices(ctypes.byref(_desc(cu)), int(chunk_size), ctypes.byref(_desc(out)),
+                                                 ctypes.byref(_lib.null_tensor()),
+                                                 ctypes.c_void_p(_stream_handle(cu.device)))
+        _lib.check(st, "cgdrPrepareChunkIndices")
+        return out
     lens = (cu_seqlens[1:] - cu_seqlens[:-1]).tolist()
     rows = [(s, c) for s, L in enumerate(lens) for c in range(math.ceil(L / chunk_size))]
     out = torch.tensor(rows, dtype=torch.int64).reshape(-1, 2)
     return out.to(cu_seqlens.device)
+
+
+def chunk_capacity(total_tokens: int, n_sequences: int, chunk_size: int = CHUNK_SIZE) -> int:
+    """Rows that always hold the chunk list of ``n_sequences`` packed into
+    ``total_tokens``: ceil(T / chunk) + N - 1 (each sequence boundary can
+    split one chunk)."""
+    return (int(total_tokens) + chunk_size - 1) // chunk_size + int(n_sequences) - 1
 
 
 def prepare_chunk_offsets(cu_seqlens: torch.Tensor, chunk_size: int = CHUNK_SIZE) -> torch.Tensor:

@@ -11,6 +11,7 @@
 
 #include "../../include/cgdr_chunk_o.h"
 #include "../../include/cgdr_gdr.h"
+#include "../../include/cgdr_varlen.h"
 #include "../../include/cgdr_wy.h"
 #include "common.cuh"
 #include "host_stages.cuh"
@@ -59,6 +60,61 @@ __global__ void __launch_bounds__(256) gdr_meta_kernel(const int32_t* asl, int64
     }
     const int64_t used = bad ? 0 : chunk_base[B];
     for (int64_t r = used + threadIdx.x; r < nt_max; r += blockDim.x) {
+        ci[2 * r] = -1;
+        ci[2 * r + 1] = -1;
+    }
+}
+
+// Chunk list from cu_seqlens (one block of 256 threads): chunk_offsets [N+1]
+// and chunk_indices [capacity, 2] with (-1, -1) padding rows.  Thread t owns a
+// contiguous range of sequences; a scan of the 256 partial chunk counts gives
+// each range its first row.  An invalid cu_seqlens (not non-decreasing from 0,
+// or more chunks than capacity) leaves every row padding.
+__global__ void __launch_bounds__(256) chunk_list_kernel(const int64_t* cu, int64_t N, int64_t chunk,
+                                                         int64_t capacity, int64_t* offsets, int64_t* ci)
+{
+    __shared__ int64_t part[256];
+    __shared__ int bad;
+    __shared__ int64_t total;
+    const int tid = threadIdx.x;
+    if (tid == 0) bad = cu[0] != 0;
+    __syncthreads();
+    const int64_t per = (N + 255) / 256;
+    const int64_t lo = tid * per, hi = lo + per < N ? lo + per : N;
+    int64_t sum = 0;
+    for (int64_t n = lo; n < hi; ++n) {
+        const int64_t L = cu[n + 1] - cu[n];
+        if (L < 0) bad = 1;
+        sum += L > 0 ? (L + chunk - 1) / chunk : 0;
+    }
+    part[tid] = sum;
+    __syncthreads();
+    if (tid == 0) {
+        int64_t run = 0;
+        for (int i = 0; i < 256; ++i) {
+            const int64_t v = part[i];
+            part[i] = run;
+            run += v;
+        }
+        if (run > capacity) bad = 1;
+        total = bad ? 0 : run;
+    }
+    __syncthreads();
+    int64_t row = part[tid];
+    for (int64_t n = lo; n < hi; ++n) {
+        const int64_t L = cu[n + 1] - cu[n];
+        const int64_t nc = L > 0 ? (L + chunk - 1) / chunk : 0;
+        if (offsets) offsets[n] = row;
+        if (!bad)
+            for (int64_t c = 0; c < nc; ++c) {
+                ci[2 * (row + c)] = n;
+                ci[2 * (row + c) + 1] = c;
+            }
+        row += nc;
+    }
+    // the last thread's running count is the total (its range is the last one)
+    if (offsets && tid == 255) offsets[N] = row;
+    for (int64_t r = total + tid; r < capacity; r += 256) {
         ci[2 * r] = -1;
         ci[2 * r + 1] = -1;
     }
@@ -344,3 +400,35 @@ cgdrStatus cgdrChunkGatedDeltaRule(void* workspace, uint64_t workspaceSize, cgdr
 }
 
 }  // extern "C"
+
+extern "C" cgdrStatus cgdrPrepareChunkIndices(const cgdrTensor* cu_seqlens, int64_t chunk_size,
+                                              const cgdrTensor* chunk_indices, const cgdrTensor* chunk_offsets,
+                                              void* stream)
+{
+    if (!present(cu_seqlens) || !present(chunk_indices))
+        return fail(CGDR_STATUS_NULL_ARGUMENT, "cu_seqlens and chunk_indices are required");
+    cgdrStatus st;
+    if ((st = check_rank(cu_seqlens, 1, "cu_seqlens")) || (st = check_rank(chunk_indices, 2, "chunk_indices"))) return st;
+    if (present(chunk_offsets) && (st = check_rank(chunk_offsets, 1, "chunk_offsets"))) return st;
+    if (cu_seqlens->dtype != CGDR_DT_INT64 || chunk_indices->dtype != CGDR_DT_INT64 ||
+        (present(chunk_offsets) && chunk_offsets->dtype != CGDR_DT_INT64))
+        return fail(CGDR_STATUS_BAD_DTYPE, "cu_seqlens, chunk_indices and chunk_offsets must be int64");
+    if (chunk_size <= 0) return fail(CGDR_STATUS_BAD_CHUNK_SIZE, "chunk_size must be positive");
+    const int64_t N = cu_seqlens->shape[0] - 1;
+    if (N < 1) return fail(CGDR_STATUS_BAD_VARLEN, "cu_seqlens needs at least two entries");
+    if (chunk_indices->shape[1] != 2) return fail(CGDR_STATUS_BAD_SHAPE, "chunk_indices must have shape [capacity, 2]");
+    if (present(chunk_offsets) && chunk_offsets->shape[0] != N + 1)
+        return fail(CGDR_STATUS_BAD_SHAPE, "chunk_offsets must have N + 1 entries");
+    if ((cu_seqlens->shape[0] > 1 && cu_seqlens->strides[0] != 1) || chunk_indices->strides[1] != 1 ||
+        chunk_indices->strides[0] != 2 || (present(chunk_offsets) && chunk_offsets->strides[0] != 1))
+        return fail(CGDR_STATUS_BAD_STRIDE, "the metadata tensors must be contiguous");
+    const int64_t capacity = chunk_indices->shape[0];
+    if (capacity == 0) return CGDR_STATUS_SUCCESS;
+    chunk_list_kernel<<<1, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const int64_t*>(cu_seqlens->data), N, chunk_size, capacity,
+        present(chunk_offsets) ? static_cast<int64_t*>(chunk_offsets->data) : nullptr,
+        static_cast<int64_t*>(chunk_indices->data));
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(CGDR_STATUS_CUDA_ERROR, "chunk list kernel launch: %s", cudaGetErrorString(e));
+    return CGDR_STATUS_SUCCESS;
+}

@@ -351,3 +351,40 @@ def test_varlen_metadata_in_workspace():
     oh, ov, of = H.oracle_run(inp, "fp32_state")
     H.assert_close(h, oh, BF_TOL, BF_TOL, "h")
     H.assert_close(f, of, BF_TOL, BF_TOL, "final (incl. the empty sequence)")
+
+
+@pytest.mark.parametrize("lens", [[5, 195, 133, 367, 0, 300, 64], [64], [1] * 300, [4096, 1, 64, 65]])
+def test_device_chunk_list_matches_the_host_list(lens):
+    """cgdrPrepareChunkIndices (no host synchronisation) gives the reference's
+    chunk list (docs/problem.txt:251-270) followed by (-1, -1) padding rows,
+    and the recurrence computes the same states from it."""
+    dev = _cuda()
+    cu_list = [0]
+    for L in lens:
+        cu_list.append(cu_list[-1] + L)
+    cu = torch.tensor(cu_list, dtype=torch.int64, device=dev)
+    cap = cg.chunk_capacity(cu_list[-1], len(lens))
+    ci_dev = cg.prepare_chunk_indices(cu, 64, capacity=cap)
+    ci_host = cg.prepare_chunk_indices(cu, 64)
+    torch.cuda.synchronize()
+    n = ci_host.shape[0]
+    assert torch.equal(ci_dev[:n], ci_host)
+    assert bool((ci_dev[n:] == -1).all())
+    if cu_list[-1] <= 4096 + 200:
+        inp = H.make_inputs(1, cu_list[-1], 2, 64, 64, seed=len(lens), cu_seqlens=cu_list)
+        t = {k: (x.to(dev) if isinstance(x, torch.Tensor) else x) for k, x in inp.items()}
+        h_pad, v_pad, f_pad = cg.chunk_gated_delta_rule_fwd_h(t["k"], t["w"], t["u"], t["g"], t["initial_state"],
+                                                              cu_seqlens=t["cu_seqlens"], chunk_indices=ci_dev,
+                                                              check_device_status=True)
+        h, v, f = cg.chunk_gated_delta_rule_fwd_h(t["k"], t["w"], t["u"], t["g"], t["initial_state"],
+                                                  cu_seqlens=t["cu_seqlens"], chunk_indices=ci_host)
+        torch.cuda.synchronize()
+        assert torch.equal(h_pad[:, :n], h) and torch.equal(v_pad, v) and torch.equal(f_pad, f)
+
+
+def test_device_chunk_list_pads_everything_for_bad_lengths():
+    dev = _cuda()
+    cu = torch.tensor([0, 100, 50], dtype=torch.int64, device=dev)  # decreasing
+    ci = cg.prepare_chunk_indices(cu, 64, capacity=8)
+    torch.cuda.synchronize()
+    assert bool((ci == -1).all())
