@@ -22,25 +22,26 @@
 // bf16 rounding of the operands.
 //
 // Persistent kernel, one CTA per SM walking tiles (chunk row, value head)
-// blockIdx.x, blockIdx.x + gridDim.x, ...  Warp roles (352 threads):
+// blockIdx.x, blockIdx.x + gridDim.x, ...  Warp roles (608 threads):
 //   warp 0      TMA producer: k and v of a tile into a STAGES-deep ring;
-//   warp 1      MMA issuer and TMEM owner (512 columns: two sets of W [64 x K]
-//               at +0 and U [64 x V] at +128, 256 apart; k k^T is written into
-//               W's first 64 columns and read before W's product overwrites it);
+//   warp 1      TMEM owner (512 columns: two sets of W [64 x K] at +0 and
+//               U [64 x V] at +128, 256 apart; k k^T is written into W's first
+//               64 columns and read before W's product overwrites it);
 //   warp 2      gate loader: beta and g of the tile (plain loads), the fp64
 //               cumulative sum, the g_c output, both into the stage;
-//   warps 3-10  two epilogue groups of four warps (one per TMEM lane quadrant:
+//   warps 3-18  two epilogue groups of eight warps (two per TMEM lane quadrant:
 //               warp w reads lanes 32(w%4).., rows 16(w%4)..+15 of an M=64
-//               accumulator).  Group g takes the tiles of accumulator set g
-//               (every other tile), so two tiles are solved at once, each group
-//               with its own scratch and named barrier.
+//               accumulator, and half of the columns).  Group g takes the tiles
+//               of accumulator set g (every other tile), so two tiles are solved
+//               at once, each group with its own scratch and named barrier.
+//               The first thread of a group issues that group's MMAs, so a
+//               group never waits on the other group's progress.
 // Per tile (stage s, accumulator set a = group):
 //   MMA   KK[a] = k k^T                       M=64 N=64 K=K (both K-major)
 //   epi   A; T (diagonal 16 x 16 blocks one per warp, then the blocks below the
 //         diagonal); T' = bf16(T diag(beta e^g_c)), T'' = bf16(T diag(beta))
 //   MMA   W[a] = T' k ; U[a] = T'' v          M=64 N=K / V K=64 (B MN-major)
-//   epi   w, u = bf16 from TMEM rows (32x32b loads) -> 16-byte stores
-// The MMA warp issues KK of tile i+1 before it waits for tile i's T.
+//   epi   w, u = bf16 from TMEM (16x256b loads, quad transpose) -> 16-byte stores
 // Every wait is bounded and no role leaves early (see kernel_chunk_o.cuh).
 #pragma once
 
@@ -85,7 +86,7 @@ template <int K_, int V_, int STAGES>
 struct WyConfig {
     static_assert(K_ == 64 || K_ == 128, "WY: K in {64, 128}");
     static_assert(V_ == 64 || V_ == 128, "WY: V in {64, 128}");
-    static constexpr int kEpiWarps = 8;
+    static constexpr int kEpiWarps = 16;  // two groups of eight
     static constexpr int kEpiThreads = 32 * kEpiWarps;
     static constexpr int kThreads = 96 + kEpiThreads;
     static constexpr int kSubK = K_ / 64;
@@ -97,13 +98,14 @@ struct WyConfig {
     static constexpr int kOffBeta = kTileK + kTileV;  // 64 fp32
     static constexpr int kOffGc = kOffBeta + 256;     // 64 fp32 (cumulative gate)
     static constexpr int kOffD = kOffGc + 256;        // 64 fp32: beta * exp(g_c), T' column factors
-    static constexpr int kStageBytes = (kOffD + 256 + 1023) / 1024 * 1024;
+    static constexpr int kOffInfo = kOffD + 256;      // WyStageInfo of the tile in this stage
+    static constexpr int kStageBytes = (kOffInfo + 32 + 1023) / 1024 * 1024;
     static constexpr int kOffT = STAGES * kStageBytes;  // [2 sets][T', T''] bf16 [64][64], 128-byte swizzle
     static constexpr int kLd = 68;                       // fp32 row stride of A and Tf
     static constexpr int kScratch = 2 * 64 * kLd * 4 + 6 * 256 * 4;  // A, Tf, Y [6][16][16] of a group
     static constexpr int kOffScratch = kOffT + 4 * 8192;             // [2 groups]
     static constexpr int kOffBar = (kOffScratch + 2 * kScratch + 1023) / 1024 * 1024;
-    static constexpr int kNumBars = 2 * STAGES + 9;
+    static constexpr int kNumBars = 2 * STAGES + 6;
     static constexpr int kUsed = kOffBar + kNumBars * 8 + 16;
     static constexpr int kSmemBytes = (kUsed + 1024 > 120 * 1024) ? kUsed + 1024 : 120 * 1024;
     static constexpr uint32_t kTmemCols = 512;
@@ -113,6 +115,12 @@ struct WyConfig {
     static constexpr uint32_t kIdescKK = umma_idesc_bf16(64, 64, false, false);
     static constexpr uint32_t kIdescW = umma_idesc_bf16(64, K_, false, true);
     static constexpr uint32_t kIdescU = umma_idesc_bf16(64, V_, false, true);
+};
+
+// The tile a stage holds, decoded once by the gate loader; `end` marks the
+// two slots after a CTA's last tile (one per epilogue group).
+struct WyStageInfo {
+    int32_t b, t0, len, hv, end;
 };
 
 struct WyTile {
@@ -176,11 +184,26 @@ __device__ __forceinline__ void quad_transpose(uint32_t (&a)[4], int lane)
     }
 }
 
-// named barrier of epilogue group g (ids 1 and 2, 128 threads each)
-__device__ __forceinline__ void wy_group_bar(int g) { asm volatile("bar.sync %0, 128;" ::"r"(1 + g) : "memory"); }
+// named barrier of epilogue group g (ids 1 and 2, 256 threads each)
+__device__ __forceinline__ void wy_group_bar(int g) { asm volatile("bar.sync %0, 256;" ::"r"(1 + g) : "memory"); }
+
+// the same barrier, returning whether `v` holds in every thread of the group
+__device__ __forceinline__ bool wy_group_bar_and(int g, bool v)
+{
+    uint32_t r;
+    asm volatile(
+        "{\n .reg .pred p, q;\n"
+        " setp.ne.u32 q, %1, 0;\n"
+        " bar.red.and.pred p, %2, 256, q;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(r)
+        : "r"(v ? 1u : 0u), "r"(1 + g)
+        : "memory");
+    return r != 0;
+}
 
 template <int K_, int V_, int STAGES>
-__global__ void __launch_bounds__(352, 1) wy_tc_kernel(const __grid_constant__ WyArgs args)
+__global__ void __launch_bounds__(608, 1) wy_tc_kernel(const __grid_constant__ WyArgs args)
 {
     using Cfg = WyConfig<K_, V_, STAGES>;
     const WyParams& p = args.p;
@@ -190,10 +213,8 @@ __global__ void __launch_bounds__(352, 1) wy_tc_kernel(const __grid_constant__ W
     uint64_t* full = bars;                 // [STAGES] k, v (TMA) + beta, g_c (gate loader)
     uint64_t* empty = bars + STAGES;       // [STAGES] W and U products done
     uint64_t* kk_full = bars + 2 * STAGES; // [2]
-    uint64_t* t_ready = kk_full + 2;       // [2]
-    uint64_t* wu_full = kk_full + 4;       // [2]
-    uint64_t* acc_empty = kk_full + 6;     // [2]
-    uint64_t* mma_drain = kk_full + 8;
+    uint64_t* wu_full = kk_full + 2;       // [2]
+    uint64_t* mma_drain = kk_full + 4;     // [2]
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Cfg::kNumBars);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     volatile int* never_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);
@@ -208,11 +229,9 @@ __global__ void __launch_bounds__(352, 1) wy_tc_kernel(const __grid_constant__ W
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&kk_full[a], 1);
-            mbar_init(&t_ready[a], 4);  // the four warps of group a
             mbar_init(&wu_full[a], 1);
-            mbar_init(&acc_empty[a], 4);
+            mbar_init(&mma_drain[a], 1);
         }
-        mbar_init(mma_drain, 1);
         *abort_flag = 0;
         *never_flag = 0;
         fence_mbarrier_init();
@@ -258,6 +277,12 @@ __global__ void __launch_bounds__(352, 1) wy_tc_kernel(const __grid_constant__ W
                                 it0, ib);
                 ++it;
             }
+            // the two end slots carry no bytes
+            for (int e = 0; e < 2 && !*abort_flag; ++e, ++it) {
+                const int s = static_cast<int>(it % STAGES);
+                if (it >= STAGES && !mbar_wait(&empty[s], (static_cast<uint32_t>(it / STAGES) - 1) & 1, ctl, 0x10)) break;
+                mbar_arrive(&full[s]);
+            }
             WaitCtl drain{never_flag, p.status, p.timeout_ns};
             for (int64_t j = it > STAGES ? it - STAGES : 0; j < it; ++j)
                 mbar_wait(&full[j % STAGES], static_cast<uint32_t>(j / STAGES) & 1, drain, 0x10);
@@ -265,6 +290,7 @@ __global__ void __launch_bounds__(352, 1) wy_tc_kernel(const __grid_constant__ W
     } else if (warp == 2) {
         // ------------------------------------------------------------ gate loader
         int64_t it = 0;
+        bool alive = true;
         for (int64_t tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x) {
             const WyTile t = wy_tile(p, tile);
             if (!t.ok) continue;
@@ -273,7 +299,10 @@ __global__ void __launch_bounds__(352, 1) wy_tc_kernel(const __grid_constant__ W
             bool go = true;
             if (it >= STAGES && lane == 0) go = mbar_wait(&empty[s], (use - 1) & 1, ctl, 0x10);
             go = __shfl_sync(0xffffffffu, go ? 1 : 0, 0) != 0;
-            if (!go) break;
+            if (!go) {
+                alive = false;
+                break;
+            }
             // rows 2*lane, 2*lane + 1; rows past the chunk's end read as beta = g = 0
             float be[2], gv[2];
 #pragma unroll
@@ -298,6 +327,10 @@ __global__ void __launch_bounds__(352, 1) wy_tc_kernel(const __grid_constant__ W
             float* sb = reinterpret_cast<float*>(smem + s * Cfg::kStageBytes + Cfg::kOffBeta);
             float* sg = reinterpret_cast<float*>(smem + s * Cfg::kStageBytes + Cfg::kOffGc);
             float* sd = reinterpret_cast<float*>(smem + s * Cfg::kStageBytes + Cfg::kOffD);
+            if (lane == 0)
+                *reinterpret_cast<WyStageInfo*>(smem + s * Cfg::kStageBytes + Cfg::kOffInfo) =
+                    WyStageInfo{static_cast<int32_t>(t.b), static_cast<int32_t>(t.t0), static_cast<int32_t>(t.len),
+                                static_cast<int32_t>(t.hv), 0};
             sb[2 * lane] = be[0];
             sb[2 * lane + 1] = be[1];
             sg[2 * lane] = c0;
@@ -311,68 +344,26 @@ __global__ void __launch_bounds__(352, 1) wy_tc_kernel(const __grid_constant__ W
             mbar_arrive(&full[s]);
             ++it;
         }
-    } else if (warp == 1) {
-        // ------------------------------------------------------------ MMA issuer
-        if (lane == 0) {
-            // W and U of tile j (stage s, set a) once its T' / T'' are ready
-            auto issue_wu = [&](int64_t j) -> bool {
-                const int s = static_cast<int>(j % STAGES);
-                const int a = static_cast<int>(j & 1);
-                if (!mbar_wait(&t_ready[a], static_cast<uint32_t>(j / 2) & 1, ctl, 0x20)) return false;
-                tc_fence_after();
-                const uint32_t st = sbase + s * Cfg::kStageBytes;
-                const uint32_t acc = tmem + a * Cfg::kAccStride;
-                const uint64_t tw = umma_desc_sw128(sbase + Cfg::kOffT + (2 * a) * 8192, 16, 1024);
-                const uint64_t tu = umma_desc_sw128(sbase + Cfg::kOffT + (2 * a + 1) * 8192, 16, 1024);
-                const uint64_t kb = umma_desc_sw128(st + Cfg::kOffK, 8192, 1024);
-                const uint64_t vb = umma_desc_sw128(st + Cfg::kOffV, 8192, 1024);
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk)
-                    tc_mma_bf16(acc, tw + static_cast<uint64_t>((kk * 32) >> 4), kb + static_cast<uint64_t>((kk * 2048) >> 4),
-                                Cfg::kIdescW, kk > 0 ? 1u : 0u);
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk)
-                    tc_mma_bf16(acc + Cfg::kTmemU, tu + static_cast<uint64_t>((kk * 32) >> 4),
-                                vb + static_cast<uint64_t>((kk * 2048) >> 4), Cfg::kIdescU, kk > 0 ? 1u : 0u);
-                tc_commit(&wu_full[a]);
-                tc_commit(&empty[s]);
-                return true;
-            };
-            int64_t it = 0;
-            bool ok = true;
-            for (int64_t tile = blockIdx.x; tile < p.n_tiles && ok; tile += gridDim.x) {
-                const WyTile t = wy_tile(p, tile);
-                if (!t.ok) continue;
-                const int s = static_cast<int>(it % STAGES);
-                const int a = static_cast<int>(it & 1);
-                const uint32_t st = sbase + s * Cfg::kStageBytes;
-                const uint32_t acc = tmem + a * Cfg::kAccStride;
-                if (!mbar_wait(&full[s], static_cast<uint32_t>(it / STAGES) & 1, ctl, 0x20)) break;
-                if (it >= 2 && !mbar_wait(&acc_empty[a], static_cast<uint32_t>(it / 2 - 1) & 1, ctl, 0x20)) break;
-                tc_fence_after();
-                {
-                    const uint64_t d = umma_desc_sw128(st + Cfg::kOffK, 16, 1024);
-#pragma unroll
-                    for (int kk = 0; kk < K_ / 16; ++kk) {
-                        const uint64_t off = static_cast<uint64_t>(((kk >> 2) * 8192 + (kk & 3) * 32) >> 4);
-                        tc_mma_bf16(acc, d + off, d + off, Cfg::kIdescKK, kk > 0 ? 1u : 0u);
-                    }
-                }
-                tc_commit(&kk_full[a]);
-                if (it >= 1) ok = issue_wu(it - 1);
-                ++it;
-            }
-            if (ok && it >= 1) issue_wu(it - 1);
-            tc_commit(mma_drain);
-            WaitCtl drain{never_flag, p.status, p.timeout_ns};
-            mbar_wait(mma_drain, 0, drain, 0x20);
+        for (int e = 0; e < 2 && alive; ++e, ++it) {
+            const int s = static_cast<int>(it % STAGES);
+            bool go = *abort_flag == 0;
+            if (go && it >= STAGES && lane == 0)
+                go = mbar_wait(&empty[s], (static_cast<uint32_t>(it / STAGES) - 1) & 1, ctl, 0x10);
+            go = __shfl_sync(0xffffffffu, go ? 1 : 0, 0) != 0;
+            if (!go) break;
+            if (lane == 0) reinterpret_cast<WyStageInfo*>(smem + s * Cfg::kStageBytes + Cfg::kOffInfo)->end = 1;
+            mbar_arrive(&full[s]);
         }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ TMEM owner
+        // (allocated above, released at the end; the groups issue their own MMAs)
     } else {
         // ------------------------------------------------------------ epilogue
-        const int grp = (warp - 3) >> 2;     // group: accumulator set, every other tile
-        const int gw = (warp - 3) & 3;       // warp within the group
-        const int gt = 32 * gw + lane;       // thread within the group, 0..127
+        const int grp = (warp - 3) >> 3;     // group: accumulator set, every other tile
+        const int gw = (warp - 3) & 7;       // warp within the group
+        const int gt = 32 * gw + lane;       // thread within the group, 0..255
         const int qd = warp & 3;             // TMEM lane quadrant
+        const int ch = gw >> 2;              // column half (two warps per quadrant)
         const int ra = 16 * qd + (lane >> 2);
         const int rb = ra + 8;
         const int pc = 2 * (lane & 3);
@@ -382,13 +373,12 @@ __global__ void __launch_bounds__(352, 1) wy_tc_kernel(const __grid_constant__ W
         float* Yb = Tf + 64 * Cfg::kLd;
         constexpr int LD = Cfg::kLd;
         const uint32_t acc = tmem + grp * Cfg::kAccStride;
+        const bool issuer = gt == 0;  // issues this group's MMAs and commits
+        const uint32_t tw_addr = sbase + Cfg::kOffT + (2 * grp) * 8192;
         bool ok = true;
-        int64_t it = 0;  // index among this CTA's valid tiles; this group takes it % 2 == grp
-        for (int64_t tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x) {
-            const WyTile t = wy_tile(p, tile);
-            if (!t.ok) continue;
-            const int64_t my = it++;
-            if ((my & 1) != grp) continue;
+        // slot `my` of the stage ring (this CTA's valid tiles in order, then two end
+        // slots); this group takes the slots my % 2 == grp
+        for (int64_t my = grp;; my += 2) {
             const int s = static_cast<int>(my % STAGES);
             const uint32_t par = static_cast<uint32_t>(my / 2) & 1;
             uint8_t* st = smem + s * Cfg::kStageBytes;
@@ -396,29 +386,48 @@ __global__ void __launch_bounds__(352, 1) wy_tc_kernel(const __grid_constant__ W
             const float* sg = reinterpret_cast<const float*>(st + Cfg::kOffGc);
             const float* sd = reinterpret_cast<const float*>(st + Cfg::kOffD);
             if (ok) ok = mbar_wait(&full[s], static_cast<uint32_t>(my / STAGES) & 1, ctl, 0x40);
+            // the whole group agrees to go on (and has finished reading the previous
+            // tile's accumulators, so KK may overwrite them)
+            tc_fence_before();
+            if (!wy_group_bar_and(grp, ok)) break;
+            const WyStageInfo info = *reinterpret_cast<const WyStageInfo*>(st + Cfg::kOffInfo);
+            if (info.end) break;
+            WyTile t;
+            t.b = info.b;
+            t.t0 = info.t0;
+            t.len = info.len;
+            t.hv = info.hv;
+            // KK = k k^T into W's first 64 columns
+            if (issuer) {
+                tc_fence_after();
+                const uint64_t d = umma_desc_sw128(sbase + s * Cfg::kStageBytes + Cfg::kOffK, 16, 1024);
+#pragma unroll
+                for (int kk = 0; kk < K_ / 16; ++kk) {
+                    const uint64_t off = static_cast<uint64_t>(((kk >> 2) * 8192 + (kk & 3) * 32) >> 4);
+                    tc_mma_bf16(acc, d + off, d + off, Cfg::kIdescKK, kk > 0 ? 1u : 0u);
+                }
+                tc_commit(&kk_full[grp]);
+            }
             if (ok) ok = mbar_wait(&kk_full[grp], par, ctl, 0x40);
             ok = __all_sync(0xffffffffu, ok) != 0;
             // ---- A = bf16(k k^T) * beta_i * exp(g_i - g_j), strictly lower, rows < len
             if (ok) {
                 tc_fence_after();
-                uint32_t kr[2][16];
-                tmem_ld_16x256b_x4(acc + ((32u * qd) << 16), kr[0]);
-                tmem_ld_16x256b_x4(acc + ((32u * qd) << 16) + 32, kr[1]);
+                uint32_t kr[16];
+                tmem_ld_16x256b_x4(acc + ((32u * qd) << 16) + 32 * ch, kr);
                 const float ba = sb[ra], bb = sb[rb], ga = sg[ra], gb = sg[rb];
                 tmem_wait_ld();
 #pragma unroll
-                for (int blk = 0; blk < 2; ++blk)
-#pragma unroll
-                    for (int jj = 0; jj < 4; ++jj)
+                for (int jj = 0; jj < 4; ++jj)
 #pragma unroll
                         for (int half = 0; half < 2; ++half) {
                             const int i = half ? rb : ra;
                             const float bi = half ? bb : ba, gi = half ? gb : ga;
-                            const int j = 32 * blk + 8 * jj + pc;
+                            const int j = 32 * ch + 8 * jj + pc;
                             float x[2];
 #pragma unroll
                             for (int bit = 0; bit < 2; ++bit) {
-                                const float kk = round_bf16(__uint_as_float(kr[blk][4 * jj + 2 * half + bit]));
+                                const float kk = round_bf16(__uint_as_float(kr[4 * jj + 2 * half + bit]));
                                 x[bit] = (j + bit < i && i < t.len)
                                              ? __fmul_rn(__fmul_rn(kk, bi), __expf(gi - sg[j + bit]))
                                              : 0.0f;
@@ -428,10 +437,10 @@ __global__ void __launch_bounds__(352, 1) wy_tc_kernel(const __grid_constant__ W
             }
             tc_fence_before();
             wy_group_bar(grp);
-            // ---- T = (I + A)^-1, diagonal blocks: warp gw owns block gw, lane c (and
+            // ---- T = (I + A)^-1, diagonal blocks: warp gw < 4 owns block gw, lane c (and
             // c + 16) column c; column-oriented forward substitution (once row r of the
             // column is final, every later row's partial sum takes its term)
-            if (ok) {
+            if (ok && gw < 4) {
                 const int b0 = 16 * gw, c = lane & 15;
                 float x[16];
 #pragma unroll
@@ -452,11 +461,12 @@ __global__ void __launch_bounds__(352, 1) wy_tc_kernel(const __grid_constant__ W
             // ---- blocks below the diagonal: B_im = T_ii A_im for the six pairs m < i,
             // then per diagonal d: T_ij = -sum_{m=j}^{i-1} B_im T_mj
             // (thread: block pair of round q, row r, columns c4..c4+3)
-            const int r = (gt >> 2) & 15, c4 = 4 * (gt & 3), sub = gt >> 6;  // two blocks per round
+            const int r = (gt >> 2) & 15, c4 = 4 * (gt & 3), sub = gt >> 6;  // four blocks per round
             if (ok) {
 #pragma unroll
-                for (int q = 0; q < 3; ++q) {
-                    const int pidx = 2 * q + sub;  // pairs (1,0) (2,0) (2,1) (3,0) (3,1) (3,2)
+                for (int q = 0; q < 2; ++q) {
+                    const int pidx = 4 * q + sub;  // pairs (1,0) (2,0) (2,1) (3,0) (3,1) (3,2)
+                    if (pidx >= 6) continue;
                     const int bi = pidx == 0 ? 1 : (pidx < 3 ? 2 : 3);
                     const int bm = pidx == 0 ? 0 : (pidx < 3 ? pidx - 1 : pidx - 3);
                     const float4* trow = reinterpret_cast<const float4*>(Tf + (16 * bi + r) * LD + 16 * bi);
@@ -484,7 +494,7 @@ __global__ void __launch_bounds__(352, 1) wy_tc_kernel(const __grid_constant__ W
 #pragma unroll
             for (int d = 1; d < 4; ++d) {
                 if (ok) {
-                    for (int bj = sub; bj < 4 - d; bj += 2) {
+                    for (int bj = sub; bj < 4 - d; bj += 4) {
                         const int bi = bj + d;
                         float4 y = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
 #pragma unroll
@@ -510,13 +520,13 @@ __global__ void __launch_bounds__(352, 1) wy_tc_kernel(const __grid_constant__ W
                 wy_group_bar(grp);
             }
             // ---- T' = bf16(T diag(beta e^g_c)), T'' = bf16(T diag(beta)) (128-byte
-            // swizzle, K-major A operands); thread: row gt/2, 32 columns
+            // swizzle, K-major A operands); thread: row gt/4, 16 columns
             if (ok) {
                 uint8_t* tw = smem + Cfg::kOffT + (2 * grp) * 8192;
                 uint8_t* tu = tw + 8192;
-                const int row = gt >> 1, cb0 = 32 * (gt & 1);
+                const int row = gt >> 2, cb0 = 16 * (gt & 3);
 #pragma unroll
-                for (int cg8 = 0; cg8 < 4; ++cg8) {
+                for (int cg8 = 0; cg8 < 2; ++cg8) {
                     const int c0 = cb0 + 8 * cg8;
                     uint32_t pw[4], pu[4];
 #pragma unroll
@@ -536,7 +546,7 @@ __global__ void __launch_bounds__(352, 1) wy_tc_kernel(const __grid_constant__ W
                     // rows of k and v past the chunk's end belong to another sequence (or
                     // are fill): zero them so that no value of theirs reaches a product
                     const int rows = kChunk - static_cast<int>(t.len);
-                    for (int e = gt; e < (Cfg::kSubK + Cfg::kSubV) * rows * 8; e += 128) {
+                    for (int e = gt; e < (Cfg::kSubK + Cfg::kSubV) * rows * 8; e += 256) {
                         const int tsub = e / (rows * 8), rr = static_cast<int>(t.len) + (e / 8) % rows, c8 = e & 7;
                         uint8_t* base = tsub < Cfg::kSubK ? st + Cfg::kOffK + tsub * 8192
                                                           : st + Cfg::kOffV + (tsub - Cfg::kSubK) * 8192;
@@ -546,8 +556,27 @@ __global__ void __launch_bounds__(352, 1) wy_tc_kernel(const __grid_constant__ W
             }
             fence_proxy_async_smem();
             tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&t_ready[grp]);
+            wy_group_bar(grp);
+            // W = T' k, U = T'' v (M=64, N=K / V, K=64; k and v MN-major); the stage
+            // is free once they complete
+            if (issuer && ok) {
+                tc_fence_after();
+                const uint32_t st = sbase + s * Cfg::kStageBytes;
+                const uint64_t tw = umma_desc_sw128(tw_addr, 16, 1024);
+                const uint64_t tu = umma_desc_sw128(tw_addr + 8192, 16, 1024);
+                const uint64_t kb = umma_desc_sw128(st + Cfg::kOffK, 8192, 1024);
+                const uint64_t vb = umma_desc_sw128(st + Cfg::kOffV, 8192, 1024);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    tc_mma_bf16(acc, tw + static_cast<uint64_t>((kk * 32) >> 4), kb + static_cast<uint64_t>((kk * 2048) >> 4),
+                                Cfg::kIdescW, kk > 0 ? 1u : 0u);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    tc_mma_bf16(acc + Cfg::kTmemU, tu + static_cast<uint64_t>((kk * 32) >> 4),
+                                vb + static_cast<uint64_t>((kk * 2048) >> 4), Cfg::kIdescU, kk > 0 ? 1u : 0u);
+                tc_commit(&wu_full[grp]);
+                tc_commit(&empty[s]);
+            }
             // ---- w, u: 16x256b fragments (thread: rows ra, rb; column pairs 2(lane%4) of
             // each 8-column group) in two batches (w, then u), a quad transpose turns the
             // pairs into 16-byte chunks (lane l%4 takes the group l%4 of every 32 columns)
@@ -559,16 +588,17 @@ __global__ void __launch_bounds__(352, 1) wy_tc_kernel(const __grid_constant__ W
                 const bool live_a = ra < t.len, live_b = rb < t.len;
 #pragma unroll
                 for (int batch = 0; batch < 2; ++batch) {
-                    constexpr int kMaxBlk = 4;
-                    const int ncols = batch == 0 ? K_ : V_;
-                    const uint32_t col0 = batch == 0 ? 0u : Cfg::kTmemU;
+                    constexpr int kMaxBlk = 2;                 // this warp: half of the columns
+                    const int ncols = (batch == 0 ? K_ : V_) / 2;
+                    const uint32_t col0 = (batch == 0 ? 0u : Cfg::kTmemU) + static_cast<uint32_t>(ncols * ch);
                     uint32_t x[kMaxBlk][16];
 #pragma unroll
                     for (int cb = 0; cb < kMaxBlk; ++cb)
                         if (cb * 32 < ncols) tmem_ld_16x256b_x4(acc + ((32u * qd) << 16) + col0 + 32 * cb, x[cb]);
                     tmem_wait_ld();
-                    __nv_bfloat16* base = batch == 0 ? p.w + t.b * p.w_sb + t.t0 * p.w_st + t.hv * p.w_sh
-                                                     : p.u + t.b * p.u_sb + t.t0 * p.u_st + t.hv * p.u_sh;
+                    __nv_bfloat16* base = (batch == 0 ? p.w + t.b * p.w_sb + t.t0 * p.w_st + t.hv * p.w_sh
+                                                      : p.u + t.b * p.u_sb + t.t0 * p.u_st + t.hv * p.u_sh) +
+                                          ncols * ch;
                     const int64_t rs = batch == 0 ? p.w_st : p.u_st;
 #pragma unroll
                     for (int cb = 0; cb < kMaxBlk; ++cb) {
@@ -589,9 +619,12 @@ __global__ void __launch_bounds__(352, 1) wy_tc_kernel(const __grid_constant__ W
                     }
                 }
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&acc_empty[grp]);
+        }
+        if (issuer) {
+            // every MMA this thread issued has completed before TMEM is released
+            tc_commit(&mma_drain[grp]);
+            WaitCtl drain{never_flag, p.status, p.timeout_ns};
+            mbar_wait(&mma_drain[grp], 0, drain, 0x20);
         }
     }
 
