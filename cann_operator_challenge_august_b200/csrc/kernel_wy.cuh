@@ -102,7 +102,8 @@ struct WyConfig {
     static constexpr int kStageBytes = (kOffInfo + 32 + 1023) / 1024 * 1024;
     static constexpr int kOffT = STAGES * kStageBytes;  // [2 sets][T', T''] bf16 [64][64], 128-byte swizzle
     static constexpr int kLd = 68;                       // fp32 row stride of A and Tf
-    static constexpr int kScratch = 2 * 64 * kLd * 4 + 6 * 256 * 4;  // A, Tf, Y [6][16][16] of a group
+    static constexpr int kLdY = 20;                      // row stride of a B block: 8 rows hit 8 banks
+    static constexpr int kScratch = 2 * 64 * kLd * 4 + 6 * 16 * kLdY * 4;  // A, Tf, Y [6][16][kLdY] of a group
     static constexpr int kOffScratch = kOffT + 4 * 8192;             // [2 groups]
     static constexpr int kOffBar = (kOffScratch + 2 * kScratch + 1023) / 1024 * 1024;
     static constexpr int kNumBars = 2 * STAGES + 6;
@@ -438,19 +439,25 @@ __global__ void __launch_bounds__(608, 1) wy_tc_kernel(const __grid_constant__ W
             tc_fence_before();
             wy_group_bar(grp);
             // ---- T = (I + A)^-1, diagonal blocks: warp gw < 4 owns block gw, lane c (and
-            // c + 16) column c; column-oriented forward substitution (once row r of the
-            // column is final, every later row's partial sum takes its term)
+            // c + 16) column c; forward substitution row by row,
+            // T[m][c] = -sum_{l<m} A[m][l] T[l][c] accumulated in increasing l (row m of
+            // A read as broadcast 16-byte loads)
             if (ok && gw < 4) {
                 const int b0 = 16 * gw, c = lane & 15;
                 float x[16];
 #pragma unroll
-                for (int r = 0; r < 16; ++r) x[r] = 0.0f;
+                for (int m = 0; m < 16; ++m) {
+                    const float4* arow = reinterpret_cast<const float4*>(Am + (b0 + m) * LD + b0);
+                    float acc = 0.0f;
 #pragma unroll
-                for (int r = 0; r < 16; ++r) {
-                    const float tr = (r == c) ? 1.0f : (r < c ? 0.0f : -x[r]);
-                    x[r] = tr;
-#pragma unroll
-                    for (int r2 = r + 1; r2 < 16; ++r2) x[r2] = fmaf(Am[(b0 + r2) * LD + b0 + r], tr, x[r2]);
+                    for (int q = 0; q < (m + 3) / 4; ++q) {
+                        const float4 a4 = arow[q];
+                        if (4 * q + 0 < m) acc = fmaf(a4.x, x[4 * q + 0], acc);
+                        if (4 * q + 1 < m) acc = fmaf(a4.y, x[4 * q + 1], acc);
+                        if (4 * q + 2 < m) acc = fmaf(a4.z, x[4 * q + 2], acc);
+                        if (4 * q + 3 < m) acc = fmaf(a4.w, x[4 * q + 3], acc);
+                    }
+                    x[m] = (m == c) ? 1.0f : (m < c ? 0.0f : -acc);
                 }
                 if (lane < 16) {
 #pragma unroll
@@ -486,7 +493,7 @@ __global__ void __launch_bounds__(608, 1) wy_tc_kernel(const __grid_constant__ W
                         acc_.z = fmaf(tk, a4.z, acc_.z);
                         acc_.w = fmaf(tk, a4.w, acc_.w);
                     }
-                    *reinterpret_cast<float4*>(Yb + pidx * 256 + r * 16 + c4) =
+                    *reinterpret_cast<float4*>(Yb + pidx * 16 * Cfg::kLdY + r * Cfg::kLdY + c4) =
                         make_float4(y[0].x + y[1].x, y[0].y + y[1].y, y[0].z + y[1].z, y[0].w + y[1].w);
                 }
             }
@@ -502,7 +509,7 @@ __global__ void __launch_bounds__(608, 1) wy_tc_kernel(const __grid_constant__ W
                             const int bm = bj + bm_off;
                             // pair index of (bi, bm): (1,0)=0 (2,0)=1 (2,1)=2 (3,0)=3 (3,1)=4 (3,2)=5
                             const int pidx = (bi * (bi - 1)) / 2 + bm;
-                            const float* brow = Yb + pidx * 256 + r * 16;
+                            const float* brow = Yb + pidx * 16 * Cfg::kLdY + r * Cfg::kLdY;
 #pragma unroll
                             for (int k = 0; k < 16; ++k) {
                                 const float bk = brow[k];
@@ -525,19 +532,23 @@ __global__ void __launch_bounds__(608, 1) wy_tc_kernel(const __grid_constant__ W
                 uint8_t* tw = smem + Cfg::kOffT + (2 * grp) * 8192;
                 uint8_t* tu = tw + 8192;
                 const int row = gt >> 2, cb0 = 16 * (gt & 3);
+                const float4* t4p = reinterpret_cast<const float4*>(Tf + row * LD + cb0);
+                const float4* b4p = reinterpret_cast<const float4*>(sb + cb0);
+                const float4* d4p = reinterpret_cast<const float4*>(sd + cb0);
 #pragma unroll
                 for (int cg8 = 0; cg8 < 2; ++cg8) {
                     const int c0 = cb0 + 8 * cg8;
                     uint32_t pw[4], pu[4];
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const int c = c0 + 2 * e;
-                        const float t0 = (c <= row) ? Tf[row * LD + c] : 0.0f;
-                        const float t1 = (c + 1 <= row) ? Tf[row * LD + c + 1] : 0.0f;
-                        const float b0 = sb[c], b1 = sb[c + 1];
-                        const float d0 = sd[c], d1 = sd[c + 1];
-                        pw[e] = pack_bf16x2(__fmul_rn(t0, d0), __fmul_rn(t1, d1));
-                        pu[e] = pack_bf16x2(__fmul_rn(t0, b0), __fmul_rn(t1, b1));
+                    for (int h = 0; h < 2; ++h) {
+                        const int c = c0 + 4 * h;  // T is lower triangular: columns past the row are 0
+                        const float4 t4 = t4p[2 * cg8 + h], b4 = b4p[2 * cg8 + h], d4 = d4p[2 * cg8 + h];
+                        const float t0 = c <= row ? t4.x : 0.0f, t1 = c + 1 <= row ? t4.y : 0.0f;
+                        const float t2 = c + 2 <= row ? t4.z : 0.0f, t3 = c + 3 <= row ? t4.w : 0.0f;
+                        pw[2 * h] = pack_bf16x2(__fmul_rn(t0, d4.x), __fmul_rn(t1, d4.y));
+                        pw[2 * h + 1] = pack_bf16x2(__fmul_rn(t2, d4.z), __fmul_rn(t3, d4.w));
+                        pu[2 * h] = pack_bf16x2(__fmul_rn(t0, b4.x), __fmul_rn(t1, b4.y));
+                        pu[2 * h + 1] = pack_bf16x2(__fmul_rn(t2, b4.z), __fmul_rn(t3, b4.w));
                     }
                     *reinterpret_cast<uint4*>(tw + sw128_off(row, c0, 8192)) = make_uint4(pw[0], pw[1], pw[2], pw[3]);
                     *reinterpret_cast<uint4*>(tu + sw128_off(row, c0, 8192)) = make_uint4(pu[0], pu[1], pu[2], pu[3]);
