@@ -11,9 +11,11 @@
 // the reference's stage 1 (ref/chunk_gated_delta_rule/tests/pytest/
 // chunk_gated_delta_rule_benchmark.py:55-83; the reference keeps -w as
 // "k_cumdecay", :74 and :82).  The inverse is restated from the mathematics
-// of a unit lower-triangular matrix: forward substitution inside the four
-// 16 x 16 diagonal blocks, then block forward substitution for the blocks
-// below the diagonal, T_ij = -T_ii sum_{m=j}^{i-1} A_im T_mj, in fp32.
+// of a unit lower-triangular matrix, in fp32: forward substitution inside the
+// four 16 x 16 diagonal blocks T_ii, then with B_im = T_ii A_im block forward
+// substitution T_ij = -sum_{m=j}^{i-1} B_im T_mj, where the three-deep block
+// T_30 is folded into two steps, T_30 = -(C_30 T_00 + C_31 T_10) with
+// C_3m = B_3m - B_32 B_2m (substituting T_20).
 //
 // The reference rounds k' = beta * exp(g_c) * k and v' = beta * v to bf16 and
 // multiplies them by bf16(T).  Here the row factors move onto T's columns:
@@ -103,7 +105,7 @@ struct WyConfig {
     static constexpr int kOffT = STAGES * kStageBytes;  // [2 sets][T', T''] bf16 [64][64], 128-byte swizzle
     static constexpr int kLd = 68;                       // fp32 row stride of A and Tf
     static constexpr int kLdY = 20;                      // row stride of a B block: 8 rows hit 8 banks
-    static constexpr int kScratch = 2 * 64 * kLd * 4 + 6 * 16 * kLdY * 4;  // A, Tf, Y [6][16][kLdY] of a group
+    static constexpr int kScratch = 2 * 64 * kLd * 4 + 7 * 16 * kLdY * 4;  // A, Tf, Y [7][16][kLdY] of a group
     static constexpr int kOffScratch = kOffT + 4 * 8192;             // [2 groups]
     static constexpr int kOffBar = (kOffScratch + 2 * kScratch + 1023) / 1024 * 1024;
     static constexpr int kNumBars = 2 * STAGES + 6;
@@ -187,6 +189,45 @@ __device__ __forceinline__ void quad_transpose(uint32_t (&a)[4], int lane)
 
 // named barrier of epilogue group g (ids 1 and 2, 256 threads each)
 __device__ __forceinline__ void wy_group_bar(int g) { asm volatile("bar.sync %0, 256;" ::"r"(1 + g) : "memory"); }
+
+__device__ __forceinline__ void fma4(float4& y, float a, const float4& b)
+{
+    y.x = fmaf(a, b.x, y.x);
+    y.y = fmaf(a, b.y, y.y);
+    y.z = fmaf(a, b.z, y.z);
+    y.w = fmaf(a, b.w, y.w);
+}
+
+// 16 x 16 block products in fp32 from shared memory (L, R: the blocks' first
+// elements, row strides in floats; 16-byte aligned rows).
+// y[h] += (L R)[r + 8h][c4..c4+3]
+__device__ __forceinline__ void wy_prod24(const float* L, int ldl, const float* R, int ldr, int r, int c4,
+                                          float4 (&y)[2])
+{
+#pragma unroll
+    for (int k4 = 0; k4 < 4; ++k4) {
+        const float4 l0 = *reinterpret_cast<const float4*>(L + r * ldl + 4 * k4);
+        const float4 l1 = *reinterpret_cast<const float4*>(L + (r + 8) * ldl + 4 * k4);
+        const float a0[4] = {l0.x, l0.y, l0.z, l0.w}, a1[4] = {l1.x, l1.y, l1.z, l1.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float4 b = *reinterpret_cast<const float4*>(R + (4 * k4 + e) * ldr + c4);
+            fma4(y[0], a0[e], b);
+            fma4(y[1], a1[e], b);
+        }
+    }
+}
+// y += (L R)[r][c4..c4+3]
+__device__ __forceinline__ void wy_prod14(const float* L, int ldl, const float* R, int ldr, int r, int c4, float4& y)
+{
+#pragma unroll
+    for (int k4 = 0; k4 < 4; ++k4) {
+        const float4 l = *reinterpret_cast<const float4*>(L + r * ldl + 4 * k4);
+        const float a[4] = {l.x, l.y, l.z, l.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) fma4(y, a[e], *reinterpret_cast<const float4*>(R + (4 * k4 + e) * ldr + c4));
+    }
+}
 
 // the same barrier, returning whether `v` holds in every thread of the group
 __device__ __forceinline__ bool wy_group_bar_and(int g, bool v)
@@ -498,34 +539,50 @@ __global__ void __launch_bounds__(608, 1) wy_tc_kernel(const __grid_constant__ W
                 }
             }
             wy_group_bar(grp);
+            // ---- block forward substitution T_ij = -sum_{m=j}^{i-1} B_im T_mj in two
+            // steps: the third diagonal is folded into the second by substituting T_20,
+            // T_30 = -(C_30 T_00 + C_31 T_10) with C_3m = B_3m - B_32 B_2m.
+            // B slots: 0 B_10, 1 B_20, 2 B_21, 3 B_30 (then C_30), 4 B_31, 5 B_32, 6 C_31.
+            auto yslot = [&](int k) { return Yb + k * 16 * Cfg::kLdY; };
+            auto tblk = [&](int bi, int bj) { return Tf + 16 * bi * LD + 16 * bj; };
+            // step 1: T_10, T_21, T_32 (two warps each, thread row r, columns c4..c4+3);
+            // C_30, C_31 (one warp each, rows r8 and r8 + 8)
+            if (ok) {
+                if (sub < 3) {
+                    const int bj = sub;  // T_{bj+1, bj} = -B_{bj+1, bj} T_{bj, bj}
+                    float4 y = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    wy_prod14(yslot(bj == 0 ? 0 : bj == 1 ? 2 : 5), Cfg::kLdY, tblk(bj, bj), LD, r, c4, y);
+                    *reinterpret_cast<float4*>(tblk(bj + 1, bj) + r * LD + c4) = make_float4(-y.x, -y.y, -y.z, -y.w);
+                } else {
+                    const int m = gw - 6, r8 = lane >> 2, c4q = 4 * (lane & 3);  // C_3m = B_3m - B_32 B_2m
+                    float4 y[2] = {};
+                    wy_prod24(yslot(5), Cfg::kLdY, yslot(1 + m), Cfg::kLdY, r8, c4q, y);
+                    const float* bsrc = yslot(3 + m);
+                    float* dst = yslot(m == 0 ? 3 : 6);
 #pragma unroll
-            for (int d = 1; d < 4; ++d) {
-                if (ok) {
-                    for (int bj = sub; bj < 4 - d; bj += 4) {
-                        const int bi = bj + d;
-                        float4 y = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-#pragma unroll
-                        for (int bm_off = 0; bm_off < d; ++bm_off) {
-                            const int bm = bj + bm_off;
-                            // pair index of (bi, bm): (1,0)=0 (2,0)=1 (2,1)=2 (3,0)=3 (3,1)=4 (3,2)=5
-                            const int pidx = (bi * (bi - 1)) / 2 + bm;
-                            const float* brow = Yb + pidx * 16 * Cfg::kLdY + r * Cfg::kLdY;
-#pragma unroll
-                            for (int k = 0; k < 16; ++k) {
-                                const float bk = brow[k];
-                                const float4 t4 = *reinterpret_cast<const float4*>(Tf + (16 * bm + k) * LD + 16 * bj + c4);
-                                y.x = fmaf(bk, t4.x, y.x);
-                                y.y = fmaf(bk, t4.y, y.y);
-                                y.z = fmaf(bk, t4.z, y.z);
-                                y.w = fmaf(bk, t4.w, y.w);
-                            }
-                        }
-                        *reinterpret_cast<float4*>(Tf + (16 * bi + r) * LD + 16 * bj + c4) =
-                            make_float4(-y.x, -y.y, -y.z, -y.w);
+                    for (int h = 0; h < 2; ++h) {
+                        const int row = r8 + 8 * h;
+                        const float4 b = *reinterpret_cast<const float4*>(bsrc + row * Cfg::kLdY + c4q);
+                        *reinterpret_cast<float4*>(dst + row * Cfg::kLdY + c4q) =
+                            make_float4(b.x - y[h].x, b.y - y[h].y, b.z - y[h].z, b.w - y[h].w);
                     }
                 }
-                wy_group_bar(grp);
             }
+            wy_group_bar(grp);
+            // step 2: T_20 = -(B_20 T_00 + B_21 T_10), T_31 = -(B_31 T_11 + B_32 T_21),
+            // T_30 = -(C_30 T_00 + C_31 T_10) (two warps each)
+            if (ok && sub < 3) {
+                const float* L1 = yslot(sub == 0 ? 1 : sub == 1 ? 4 : 3);
+                const float* L2 = yslot(sub == 0 ? 2 : sub == 1 ? 5 : 6);
+                const float* R1 = sub == 1 ? tblk(1, 1) : tblk(0, 0);
+                const float* R2 = sub == 1 ? tblk(2, 1) : tblk(1, 0);
+                float4 y = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                wy_prod14(L1, Cfg::kLdY, R1, LD, r, c4, y);
+                wy_prod14(L2, Cfg::kLdY, R2, LD, r, c4, y);
+                float* D = sub == 0 ? tblk(2, 0) : sub == 1 ? tblk(3, 1) : tblk(3, 0);
+                *reinterpret_cast<float4*>(D + r * LD + c4) = make_float4(-y.x, -y.y, -y.z, -y.w);
+            }
+            wy_group_bar(grp);
             // ---- T' = bf16(T diag(beta e^g_c)), T'' = bf16(T diag(beta)) (128-byte
             // swizzle, K-major A operands); thread: row gt/4, 16 columns
             if (ok) {
