@@ -362,14 +362,8 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
             const bool partial_varlen = p.varlen && len < kChunk;
 
             // ================= epilogue 1 =================
-            if (!mbar_wait(mma1_done, static_cast<uint32_t>(c) & 1, ctl, 0x40)) { ok = false; break; }
+            // The gates and the u loads need only the stage: they run while MMA1 does.
             if (!mbar_wait(&full[s], static_cast<uint32_t>(c / STAGES) & 1, ctl, 0x40)) { ok = false; break; }
-            tc_fence_after();
-            uint32_t acc[Cfg::kCW / 32][16];
-#pragma unroll
-            for (int cb = 0; cb < Cfg::kCW / 32; ++cb)
-                tmem_ld_16x256b_x4(tmem + ((32u * q) << 16) + static_cast<uint32_t>(cbase + 32 * cb), acc[cb]);
-            tmem_wait_ld();
             const float* gs = reinterpret_cast<const float*>(smem + Cfg::kOffG) + 64 * s;
             float g_l = 0.f, g_a = 0.f, g_b = 0.f;
             if (p.g) {
@@ -403,6 +397,13 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
             uint32_t uraw[kPairs], vds[kPairs], vns[kPairs], vos[kPairs];
 #pragma unroll
             for (int i = 0; i < kPairs; ++i) uraw[i] = *reinterpret_cast<const uint32_t*>(ut + offs[i]);
+            if (!mbar_wait(mma1_done, static_cast<uint32_t>(c) & 1, ctl, 0x40)) { ok = false; break; }
+            tc_fence_after();
+            uint32_t acc[Cfg::kCW / 32][16];
+#pragma unroll
+            for (int cb = 0; cb < Cfg::kCW / 32; ++cb)
+                tmem_ld_16x256b_x4(tmem + ((32u * q) << 16) + static_cast<uint32_t>(cbase + 32 * cb), acc[cb]);
+            tmem_wait_ld();
             // v_decay only (the MMA2 operand); v_new is packed after MMA2 is released.
             bool packed_ref = false;
             if (ref) {
