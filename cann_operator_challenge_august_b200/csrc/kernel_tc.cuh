@@ -233,27 +233,35 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
         }
     } else if (warp == Cfg::kMmaWarp) {
         // ------------------------------------------------------------ MMA issuer
-        if (lane == 0) {
-            const uint32_t d1 = tmem;
-            const uint32_t d2 = tmem + VT;
-            const uint32_t s_addr = sbase + Cfg::kOffS;
-            for (int64_t c = 0; c < nchunks; ++c) {
-                const int s = static_cast<int>(c % STAGES);
-                if (!mbar_wait(&full[s], static_cast<uint32_t>(c / STAGES) & 1, ctl, 0x20)) break;
-                if (!mbar_wait(s_ready, static_cast<uint32_t>(c) & 1, ctl, 0x20)) break;
-                tc_fence_after();
-                // descriptors differ only in the start-address field (bits 0-13, 16-byte units)
-                const uint64_t a1 = umma_desc_sw128(wc_addr(s), 16, 1024);
-                const uint64_t b1 = umma_desc_sw128(s_addr, Cfg::kSSubBytes, 1024);
+        // The whole warp runs the loop (descriptors stay warp-uniform); one elected
+        // lane issues each MMA and commit, so issue does not stall on a divergent branch.
+        auto wait_warp = [&](uint64_t* bar, uint32_t parity) {
+            return __all_sync(0xffffffffu, mbar_wait(bar, parity, ctl, 0x20) ? 1 : 0) != 0;
+        };
+        const uint32_t d1 = tmem;
+        const uint32_t d2 = tmem + VT;
+        const uint32_t s_addr = sbase + Cfg::kOffS;
+        for (int64_t c = 0; c < nchunks; ++c) {
+            const int s = static_cast<int>(c % STAGES);
+            if (!wait_warp(&full[s], static_cast<uint32_t>(c / STAGES) & 1)) break;
+            if (!wait_warp(s_ready, static_cast<uint32_t>(c) & 1)) break;
+            tc_fence_after();
+            // descriptors differ only in the start-address field (bits 0-13, 16-byte units)
+            const uint64_t a1 = umma_desc_sw128(wc_addr(s), 16, 1024);
+            const uint64_t b1 = umma_desc_sw128(s_addr, Cfg::kSSubBytes, 1024);
+            if (elect_one_sync()) {
 #pragma unroll
                 for (int kk = 0; kk < K_ / 16; ++kk)
                     tc_mma_bf16(d1, a1 + static_cast<uint64_t>(((kk >> 2) * 8192 + (kk & 3) * 32) >> 4),
                                 b1 + static_cast<uint64_t>((kk * 2048) >> 4), Cfg::kIdesc1, kk > 0 ? 1u : 0u);
                 tc_commit(mma1_done);
-                if (!mbar_wait(vdec_ready, static_cast<uint32_t>(c) & 1, ctl, 0x20)) break;
-                tc_fence_after();
-                const uint64_t a2 = umma_desc_sw128(kc_addr(s), 8192, 1024);
-                const uint64_t b2 = umma_desc_sw128(uc_addr(s), 8192, 1024);
+            }
+            __syncwarp();
+            if (!wait_warp(vdec_ready, static_cast<uint32_t>(c) & 1)) break;
+            tc_fence_after();
+            const uint64_t a2 = umma_desc_sw128(kc_addr(s), 8192, 1024);
+            const uint64_t b2 = umma_desc_sw128(uc_addr(s), 8192, 1024);
+            if (elect_one_sync()) {
 #pragma unroll
                 for (int tt = 0; tt < 4; ++tt)
                     tc_mma_bf16(d2, a2 + static_cast<uint64_t>((tt * 2048) >> 4), b2 + static_cast<uint64_t>((tt * 2048) >> 4),
@@ -261,12 +269,14 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
                 tc_commit(mma2_done);
                 tc_commit(&empty[s]);
             }
-            // Drain: every MMA this thread issued has completed before the
-            // TMEM it writes is released (matters only on an abort path).
-            tc_commit(mma_drain);
-            WaitCtl drain{never_flag, p.status, p.timeout_ns};
-            mbar_wait(mma_drain, 0, drain, 0x20);
+            __syncwarp();
         }
+        // Drain: every MMA this warp issued has completed before the TMEM it writes
+        // is released (matters only on an abort path).
+        if (elect_one_sync()) tc_commit(mma_drain);
+        __syncwarp();
+        WaitCtl drain{never_flag, p.status, p.timeout_ns};
+        mbar_wait(mma_drain, 0, drain, 0x20);
     } else {
         // ------------------------------------------------------------ epilogue
         const int q = warp & 3;          // TMEM lane quadrant
