@@ -265,55 +265,61 @@ __global__ void __launch_bounds__(320, 1) chunk_o_tc_kernel(const __grid_constan
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
-        if (lane == 0) {
-            int64_t it = 0;
-            for (int64_t tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x) {
-                const ChunkOTile t = chunk_o_tile(p, tile, VT);
-                if (!t.ok) continue;
-                const int s = static_cast<int>(it % STAGES);
-                const int a = static_cast<int>(it & 1);
-                const uint32_t st = sbase + s * Cfg::kStageBytes;
-                const uint32_t acc = tmem + a * Cfg::kAccStride;
-                if (!mbar_wait(&full[s], static_cast<uint32_t>(it / STAGES) & 1, ctl, 0x20)) break;
-                if (it >= 2 && !mbar_wait(&acc_empty[a], static_cast<uint32_t>(it / 2 - 1) & 1, ctl, 0x20)) break;
-                tc_fence_after();
-                {
-                    const uint64_t da = umma_desc_sw128(st + Cfg::kOffQ, 16, 1024);
-                    const uint64_t db = umma_desc_sw128(st + Cfg::kOffK, 16, 1024);
+        // The whole warp runs the loop; one elected lane issues the MMAs and commits.
+        auto wait_warp = [&](uint64_t* bar, uint32_t parity) {
+            return __all_sync(0xffffffffu, mbar_wait(bar, parity, ctl, 0x20) ? 1 : 0) != 0;
+        };
+        int64_t it = 0;
+        for (int64_t tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x) {
+            const ChunkOTile t = chunk_o_tile(p, tile, VT);
+            if (!t.ok) continue;
+            const int s = static_cast<int>(it % STAGES);
+            const int a = static_cast<int>(it & 1);
+            const uint32_t st = sbase + s * Cfg::kStageBytes;
+            const uint32_t acc = tmem + a * Cfg::kAccStride;
+            if (!wait_warp(&full[s], static_cast<uint32_t>(it / STAGES) & 1)) break;
+            if (it >= 2 && !wait_warp(&acc_empty[a], static_cast<uint32_t>(it / 2 - 1) & 1)) break;
+            tc_fence_after();
+            {
+                const uint64_t da = umma_desc_sw128(st + Cfg::kOffQ, 16, 1024);
+                const uint64_t db = umma_desc_sw128(st + Cfg::kOffK, 16, 1024);
+                const uint64_t dh = umma_desc_sw128(st + Cfg::kOffH, Cfg::kHSub, 1024);
+                if (elect_one_sync()) {
 #pragma unroll
                     for (int kk = 0; kk < K_ / 16; ++kk) {
                         const uint64_t off = static_cast<uint64_t>(((kk >> 2) * 8192 + (kk & 3) * 32) >> 4);
                         tc_mma_bf16(acc + Cfg::kTmemS, da + off, db + off, Cfg::kIdescS, kk > 0 ? 1u : 0u);
                     }
-                }
-                tc_commit(&s_full[a]);
-                {
-                    const uint64_t da = umma_desc_sw128(st + Cfg::kOffQ, 16, 1024);
-                    const uint64_t db = umma_desc_sw128(st + Cfg::kOffH, Cfg::kHSub, 1024);
+                    tc_commit(&s_full[a]);
 #pragma unroll
                     for (int kk = 0; kk < K_ / 16; ++kk)
                         tc_mma_bf16(acc, da + static_cast<uint64_t>(((kk >> 2) * 8192 + (kk & 3) * 32) >> 4),
-                                    db + static_cast<uint64_t>((kk * 2048) >> 4), Cfg::kIdescO, kk > 0 ? 1u : 0u);
+                                    dh + static_cast<uint64_t>((kk * 2048) >> 4), Cfg::kIdescO, kk > 0 ? 1u : 0u);
+                    tc_commit(&o1_full[a]);
                 }
-                tc_commit(&o1_full[a]);
-                if (!mbar_wait(&p_ready[a], static_cast<uint32_t>(it / 2) & 1, ctl, 0x20)) break;
-                tc_fence_after();
-                {
-                    const uint64_t pa = umma_desc_sw128(st + Cfg::kOffK, 16, 1024);
-                    const uint64_t vb = umma_desc_sw128(st + Cfg::kOffV, 8192, 1024);
+                __syncwarp();
+            }
+            if (!wait_warp(&p_ready[a], static_cast<uint32_t>(it / 2) & 1)) break;
+            tc_fence_after();
+            {
+                const uint64_t pa = umma_desc_sw128(st + Cfg::kOffK, 16, 1024);
+                const uint64_t vb = umma_desc_sw128(st + Cfg::kOffV, 8192, 1024);
+                if (elect_one_sync()) {
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk)
                         tc_mma_bf16(acc, pa + static_cast<uint64_t>((kk * 32) >> 4),
                                     vb + static_cast<uint64_t>((kk * 2048) >> 4), Cfg::kIdescO, 1u);
+                    tc_commit(&o_full[a]);
+                    tc_commit(&empty[s]);
                 }
-                tc_commit(&o_full[a]);
-                tc_commit(&empty[s]);
-                ++it;
+                __syncwarp();
             }
-            tc_commit(mma_drain);
-            WaitCtl drain{never_flag, p.status, p.timeout_ns};
-            mbar_wait(mma_drain, 0, drain, 0x20);
+            ++it;
         }
+        if (elect_one_sync()) tc_commit(mma_drain);
+        __syncwarp();
+        WaitCtl drain{never_flag, p.status, p.timeout_ns};
+        mbar_wait(mma_drain, 0, drain, 0x20);
     } else {
         // ------------------------------------------------------------ epilogue
         const int et = threadIdx.x - 64;     // 0..255

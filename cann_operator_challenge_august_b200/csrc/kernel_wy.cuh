@@ -36,8 +36,8 @@
 //               accumulator, and half of the columns).  Group g takes the tiles
 //               of accumulator set g (every other tile), so two tiles are solved
 //               at once, each group with its own scratch and named barrier.
-//               The first thread of a group issues that group's MMAs, so a
-//               group never waits on the other group's progress.
+//               The group's first warp issues that group's MMAs (one elected
+//               lane), so a group never waits on the other group's progress.
 // Per tile (stage s, accumulator set a = group):
 //   MMA   KK[a] = k k^T                       M=64 N=64 K=K (both K-major)
 //   epi   A; T (diagonal 16 x 16 blocks one per warp, then the blocks below the
@@ -415,7 +415,9 @@ __global__ void __launch_bounds__(608, 1) wy_tc_kernel(const __grid_constant__ W
         float* Yb = Tf + 64 * Cfg::kLd;
         constexpr int LD = Cfg::kLd;
         const uint32_t acc = tmem + grp * Cfg::kAccStride;
-        const bool issuer = gt == 0;  // issues this group's MMAs and commits
+        // the group's first warp issues its MMAs and commits: the whole warp runs that
+        // code (warp-uniform descriptors) and one elected lane issues
+        const bool issuer = gw == 0;
         const uint32_t tw_addr = sbase + Cfg::kOffT + (2 * grp) * 8192;
         bool ok = true;
         // slot `my` of the stage ring (this CTA's valid tiles in order, then two end
@@ -443,12 +445,15 @@ __global__ void __launch_bounds__(608, 1) wy_tc_kernel(const __grid_constant__ W
             if (issuer) {
                 tc_fence_after();
                 const uint64_t d = umma_desc_sw128(sbase + s * Cfg::kStageBytes + Cfg::kOffK, 16, 1024);
+                if (elect_one_sync()) {
 #pragma unroll
-                for (int kk = 0; kk < K_ / 16; ++kk) {
-                    const uint64_t off = static_cast<uint64_t>(((kk >> 2) * 8192 + (kk & 3) * 32) >> 4);
-                    tc_mma_bf16(acc, d + off, d + off, Cfg::kIdescKK, kk > 0 ? 1u : 0u);
+                    for (int kk = 0; kk < K_ / 16; ++kk) {
+                        const uint64_t off = static_cast<uint64_t>(((kk >> 2) * 8192 + (kk & 3) * 32) >> 4);
+                        tc_mma_bf16(acc, d + off, d + off, Cfg::kIdescKK, kk > 0 ? 1u : 0u);
+                    }
+                    tc_commit(&kk_full[grp]);
                 }
-                tc_commit(&kk_full[grp]);
+                __syncwarp();
             }
             if (ok) ok = mbar_wait(&kk_full[grp], par, ctl, 0x40);
             ok = __all_sync(0xffffffffu, ok) != 0;
@@ -634,16 +639,19 @@ __global__ void __launch_bounds__(608, 1) wy_tc_kernel(const __grid_constant__ W
                 const uint64_t tu = umma_desc_sw128(tw_addr + 8192, 16, 1024);
                 const uint64_t kb = umma_desc_sw128(st + Cfg::kOffK, 8192, 1024);
                 const uint64_t vb = umma_desc_sw128(st + Cfg::kOffV, 8192, 1024);
+                if (elect_one_sync()) {
 #pragma unroll
-                for (int kk = 0; kk < 4; ++kk)
-                    tc_mma_bf16(acc, tw + static_cast<uint64_t>((kk * 32) >> 4), kb + static_cast<uint64_t>((kk * 2048) >> 4),
-                                Cfg::kIdescW, kk > 0 ? 1u : 0u);
+                    for (int kk = 0; kk < 4; ++kk)
+                        tc_mma_bf16(acc, tw + static_cast<uint64_t>((kk * 32) >> 4),
+                                    kb + static_cast<uint64_t>((kk * 2048) >> 4), Cfg::kIdescW, kk > 0 ? 1u : 0u);
 #pragma unroll
-                for (int kk = 0; kk < 4; ++kk)
-                    tc_mma_bf16(acc + Cfg::kTmemU, tu + static_cast<uint64_t>((kk * 32) >> 4),
-                                vb + static_cast<uint64_t>((kk * 2048) >> 4), Cfg::kIdescU, kk > 0 ? 1u : 0u);
-                tc_commit(&wu_full[grp]);
-                tc_commit(&empty[s]);
+                    for (int kk = 0; kk < 4; ++kk)
+                        tc_mma_bf16(acc + Cfg::kTmemU, tu + static_cast<uint64_t>((kk * 32) >> 4),
+                                    vb + static_cast<uint64_t>((kk * 2048) >> 4), Cfg::kIdescU, kk > 0 ? 1u : 0u);
+                    tc_commit(&wu_full[grp]);
+                    tc_commit(&empty[s]);
+                }
+                __syncwarp();
             }
             // ---- w, u: 16x256b fragments (thread: rows ra, rb; column pairs 2(lane%4) of
             // each 8-column group) in two batches (w, then u), a quad transpose turns the
@@ -689,8 +697,9 @@ __global__ void __launch_bounds__(608, 1) wy_tc_kernel(const __grid_constant__ W
             }
         }
         if (issuer) {
-            // every MMA this thread issued has completed before TMEM is released
-            tc_commit(&mma_drain[grp]);
+            // every MMA this warp issued has completed before TMEM is released
+            if (elect_one_sync()) tc_commit(&mma_drain[grp]);
+            __syncwarp();
             WaitCtl drain{never_flag, p.status, p.timeout_ns};
             mbar_wait(&mma_drain[grp], 0, drain, 0x20);
         }
