@@ -120,6 +120,70 @@ __global__ void __launch_bounds__(256) chunk_list_kernel(const int64_t* cu, int6
     }
 }
 
+// Zero-padding of the head dimension for Dk, Dv outside {64, 128}: the
+// kernels run at the next supported width and the padded columns carry exact
+// zeros through every product and sum (k k^T, T' k, w S, k^T v_dec, q S), so
+// the result equals the unpadded arithmetic.
+//   src [R0, R1, D] (strides s0, s1, 1) -> dst [R0, R1, Dp] contiguous, zeros past D
+__global__ void __launch_bounds__(256) pad_heads_kernel(const __nv_bfloat16* src, int64_t s0, int64_t s1, int64_t R0,
+                                                        int64_t R1, int64_t D, __nv_bfloat16* dst, int64_t Dp)
+{
+    const int64_t n = R0 * R1 * Dp;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t d = i % Dp, r = i / Dp, r1 = r % R1, r0 = r / R1;
+        dst[i] = d < D ? src[r0 * s0 + r1 * s1 + d] : __float2bfloat16(0.0f);
+    }
+}
+
+//   dst [R0, R1, D] (strides s0, s1, 1) <- src [R0, R1, Dp] contiguous, first D columns
+__global__ void __launch_bounds__(256) unpad_heads_kernel(const __nv_bfloat16* src, int64_t Dp, int64_t R0, int64_t R1,
+                                                          int64_t D, __nv_bfloat16* dst, int64_t s0, int64_t s1)
+{
+    const int64_t n = R0 * R1 * D;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t d = i % D, r = i / D, r1 = r % R1, r0 = r / R1;
+        dst[r0 * s0 + r1 * s1 + d] = src[r * Dp + d];
+    }
+}
+
+// states: [B, Nv, Dv, Dk] (any strides, bf16 or fp32) <-> [B, Nv, Kp, Vp] fp32 contiguous
+__global__ void __launch_bounds__(256) pad_state_kernel(const void* src, int32_t dt, int64_t s0, int64_t s1, int64_t sv,
+                                                        int64_t sk, int64_t B, int64_t Nv, int64_t Dv, int64_t Dk,
+                                                        float* dst, int64_t Kp, int64_t Vp)
+{
+    const int64_t n = B * Nv * Kp * Vp;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t vv = i % Vp, kk = (i / Vp) % Kp, bn = i / (Vp * Kp), nn = bn % Nv, b = bn / Nv;
+        float x = 0.0f;
+        if (kk < Dk && vv < Dv) {
+            const int64_t at = b * s0 + nn * s1 + vv * sv + kk * sk;
+            x = dt == CGDR_DT_FLOAT32 ? static_cast<const float*>(src)[at]
+                                      : __bfloat162float(static_cast<const __nv_bfloat16*>(src)[at]);
+        }
+        dst[i] = x;
+    }
+}
+
+__global__ void __launch_bounds__(256) unpad_state_kernel(const float* src, int64_t Kp, int64_t Vp, int64_t B,
+                                                          int64_t Nv, int64_t Dv, int64_t Dk, void* dst, int32_t dt,
+                                                          int64_t s0, int64_t s1, int64_t sv, int64_t sk)
+{
+    const int64_t n = B * Nv * Dv * Dk;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t kk = i % Dk, vv = (i / Dk) % Dv, bn = i / (Dk * Dv), nn = bn % Nv, b = bn / Nv;
+        const float x = src[((b * Nv + nn) * Kp + kk) * Vp + vv];
+        const int64_t at = b * s0 + nn * s1 + vv * sv + kk * sk;
+        if (dt == CGDR_DT_FLOAT32)
+            static_cast<float*>(dst)[at] = x;
+        else
+            static_cast<__nv_bfloat16*>(dst)[at] = __float2bfloat16_rn(x);
+    }
+}
+
 }  // namespace cgdr
 
 struct cgdrGdrExecutor {
@@ -128,8 +192,10 @@ struct cgdrGdrExecutor {
     bool has_g;
     float scale;
     int64_t B, T, Nk, Nv, Dk, Dv, nt_max;
+    int64_t Kp, Vp;  // head widths the kernels run at (Dk, Dv padded up to 64 or 128)
     // workspace layout (byte offsets)
     uint64_t off_cu, off_cb, off_ci, off_meta, off_gc, off_w, off_u, off_vn, off_h, total;
+    uint64_t off_qp, off_kp, off_vp, off_op, off_h0p, off_finp;  // padding buffers (Kp != Dk or Vp != Dv)
 };
 
 namespace {
@@ -237,12 +303,15 @@ cgdrStatus build_gdr(const cgdrTensor* q, const cgdrTensor* k, const cgdrTensor*
     // empty tensors (tiling.cpp:567-590)
     for (const cgdrTensor* t : {q, k, v, beta, h0, asl, out, fin})
         if (has_empty(t)) return fail(CGDR_STATUS_BAD_SHAPE, "empty tensors are not supported");
-    // this build
-    if (!(Dk == 64 || Dk == 128) || !(Dv == 64 || Dv == 128))
-        return fail(CGDR_STATUS_UNSUPPORTED, "this build computes Dk and Dv in {64, 128}, got Dk=%lld, Dv=%lld",
-                    (long long)Dk, (long long)Dv);
-    for (const cgdrTensor* t : {q, k, v, out})
-        if (!sixteen(t))
+    // the kernels run at Dk, Dv in {64, 128}; other widths go through zero-padded copies
+    const int64_t Kp = Dk <= 64 ? 64 : 128, Vp = Dv <= 64 ? 64 : 128;
+    const bool padK = Kp != Dk, padV = Vp != Dv;
+    for (const cgdrTensor* t : {q, k})
+        if (t->strides[2] != 1 || (!padK && !sixteen(t)))
+            return fail(CGDR_STATUS_BAD_STRIDE,
+                        "query, key, value and out need a contiguous last dimension and 16-byte aligned strides");
+    for (const cgdrTensor* t : {v, out})
+        if (t->strides[2] != 1 || (!padV && !sixteen(t)))
             return fail(CGDR_STATUS_BAD_STRIDE,
                         "query, key, value and out need a contiguous last dimension and 16-byte aligned strides");
     if (asl->strides[0] != 1 && B > 1) return fail(CGDR_STATUS_BAD_STRIDE, "actualSeqLengths must be contiguous");
@@ -257,6 +326,7 @@ cgdrStatus build_gdr(const cgdrTensor* q, const cgdrTensor* k, const cgdrTensor*
     if (has_g) ex->g = *g;
     ex->scale = scale > 0.0f ? scale : static_cast<float>(1.0 / std::sqrt(static_cast<double>(Dk)));
     ex->B = B; ex->T = T; ex->Nk = Nk; ex->Nv = Nv; ex->Dk = Dk; ex->Dv = Dv;
+    ex->Kp = Kp; ex->Vp = Vp;
     ex->nt_max = (T + kChunk - 1) / kChunk + B - 1;
     uint64_t off = kHeader;
     auto take = [&](uint64_t bytes) {
@@ -270,10 +340,23 @@ cgdrStatus build_gdr(const cgdrTensor* q, const cgdrTensor* k, const cgdrTensor*
     // the recurrence's varlen metadata: chunk base [N+1] and launch order [N], int32
     ex->off_meta = take(align256(4 * static_cast<uint64_t>(B + 1)) + align256(4 * static_cast<uint64_t>(B)));
     ex->off_gc = take(4 * static_cast<uint64_t>(T * Nv));
-    ex->off_w = take(2 * static_cast<uint64_t>(T * Nv * Dk));
-    ex->off_u = take(2 * static_cast<uint64_t>(T * Nv * Dv));
-    ex->off_vn = take(2 * static_cast<uint64_t>(T * Nv * Dv));
-    ex->off_h = take(2 * static_cast<uint64_t>(ex->nt_max * Nv * Dk * Dv));
+    ex->off_w = take(2 * static_cast<uint64_t>(T * Nv * Kp));
+    ex->off_u = take(2 * static_cast<uint64_t>(T * Nv * Vp));
+    ex->off_vn = take(2 * static_cast<uint64_t>(T * Nv * Vp));
+    ex->off_h = take(2 * static_cast<uint64_t>(ex->nt_max * Nv * Kp * Vp));
+    ex->off_qp = ex->off_kp = ex->off_vp = ex->off_op = ex->off_h0p = ex->off_finp = 0;
+    if (padK) {
+        ex->off_qp = take(2 * static_cast<uint64_t>(T * Nk * Kp));
+        ex->off_kp = take(2 * static_cast<uint64_t>(T * Nk * Kp));
+    }
+    if (padV) {
+        ex->off_vp = take(2 * static_cast<uint64_t>(T * Nv * Vp));
+        ex->off_op = take(2 * static_cast<uint64_t>(T * Nv * Vp));
+    }
+    if (padK || padV) {
+        ex->off_h0p = take(4 * static_cast<uint64_t>(B * Nv * Kp * Vp));
+        ex->off_finp = take(4 * static_cast<uint64_t>(B * Nv * Kp * Vp));
+    }
     ex->total = off;
     *ws_size = off;
     *exo = ex;
@@ -321,27 +404,36 @@ cgdrStatus cgdrChunkGatedDeltaRule(void* workspace, uint64_t workspaceSize, cgdr
     cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     int* status = reinterpret_cast<int*>(ws);
-    const int64_t T = ex.T, Nk = ex.Nk, Nv = ex.Nv, Dk = ex.Dk, Dv = ex.Dv, B = ex.B, NT = ex.nt_max;
+    const int64_t T = ex.T, Nk = ex.Nk, Nv = ex.Nv, B = ex.B, NT = ex.nt_max;
+    const int64_t Dk = ex.Kp, Dv = ex.Vp;  // the widths the kernels run at
+    const bool padK = ex.Kp != ex.Dk, padV = ex.Vp != ex.Dv, padS = padK || padV;
 
     // views: the TND tensors as [1, T, heads, dim] (a packed varlen batch), the
-    // [B, Nv, Dv, Dk] states as [B, Nv, K=Dk, V=Dv] by their strides
-    const cgdrTensor q4 = view(ex.q.data, CGDR_DT_BF16, {1, T, Nk, Dk},
-                               {T * ex.q.strides[0], ex.q.strides[0], ex.q.strides[1], ex.q.strides[2]});
-    const cgdrTensor k4 = view(ex.k.data, CGDR_DT_BF16, {1, T, Nk, Dk},
-                               {T * ex.k.strides[0], ex.k.strides[0], ex.k.strides[1], ex.k.strides[2]});
-    const cgdrTensor v4 = view(ex.v.data, CGDR_DT_BF16, {1, T, Nv, Dv},
-                               {T * ex.v.strides[0], ex.v.strides[0], ex.v.strides[1], ex.v.strides[2]});
-    const cgdrTensor o4 = view(ex.out.data, CGDR_DT_BF16, {1, T, Nv, Dv},
-                               {T * ex.out.strides[0], ex.out.strides[0], ex.out.strides[1], ex.out.strides[2]});
+    // [B, Nv, Dv, Dk] states as [B, Nv, K=Dk, V=Dv] by their strides; padded
+    // copies in the workspace where a width is not 64 or 128
+    const cgdrTensor q4 = padK ? contiguous(ws + ex.off_qp, CGDR_DT_BF16, {1, T, Nk, Dk})
+                               : view(ex.q.data, CGDR_DT_BF16, {1, T, Nk, Dk},
+                                      {T * ex.q.strides[0], ex.q.strides[0], ex.q.strides[1], ex.q.strides[2]});
+    const cgdrTensor k4 = padK ? contiguous(ws + ex.off_kp, CGDR_DT_BF16, {1, T, Nk, Dk})
+                               : view(ex.k.data, CGDR_DT_BF16, {1, T, Nk, Dk},
+                                      {T * ex.k.strides[0], ex.k.strides[0], ex.k.strides[1], ex.k.strides[2]});
+    const cgdrTensor v4 = padV ? contiguous(ws + ex.off_vp, CGDR_DT_BF16, {1, T, Nv, Dv})
+                               : view(ex.v.data, CGDR_DT_BF16, {1, T, Nv, Dv},
+                                      {T * ex.v.strides[0], ex.v.strides[0], ex.v.strides[1], ex.v.strides[2]});
+    const cgdrTensor o4 = padV ? contiguous(ws + ex.off_op, CGDR_DT_BF16, {1, T, Nv, Dv})
+                               : view(ex.out.data, CGDR_DT_BF16, {1, T, Nv, Dv},
+                                      {T * ex.out.strides[0], ex.out.strides[0], ex.out.strides[1], ex.out.strides[2]});
     const cgdrTensor b3 = view(ex.beta.data, CGDR_DT_BF16, {1, T, Nv},
                                {T * ex.beta.strides[0], ex.beta.strides[0], ex.beta.strides[1]});
     cgdrTensor g3;
     memset(&g3, 0, sizeof(g3));
     if (ex.has_g) g3 = view(ex.g.data, CGDR_DT_FLOAT32, {1, T, Nv}, {T * ex.g.strides[0], ex.g.strides[0], ex.g.strides[1]});
-    const cgdrTensor h0 = view(ex.h0.data, ex.h0.dtype, {B, Nv, Dk, Dv},
-                               {ex.h0.strides[0], ex.h0.strides[1], ex.h0.strides[3], ex.h0.strides[2]});
-    const cgdrTensor fin = view(ex.fin.data, ex.fin.dtype, {B, Nv, Dk, Dv},
-                                {ex.fin.strides[0], ex.fin.strides[1], ex.fin.strides[3], ex.fin.strides[2]});
+    const cgdrTensor h0 = padS ? contiguous(ws + ex.off_h0p, CGDR_DT_FLOAT32, {B, Nv, Dk, Dv})
+                               : view(ex.h0.data, ex.h0.dtype, {B, Nv, Dk, Dv},
+                                      {ex.h0.strides[0], ex.h0.strides[1], ex.h0.strides[3], ex.h0.strides[2]});
+    const cgdrTensor fin = padS ? contiguous(ws + ex.off_finp, CGDR_DT_FLOAT32, {B, Nv, Dk, Dv})
+                                : view(ex.fin.data, ex.fin.dtype, {B, Nv, Dk, Dv},
+                                       {ex.fin.strides[0], ex.fin.strides[1], ex.fin.strides[3], ex.fin.strides[2]});
     // workspace tensors
     const cgdrTensor cu = contiguous(ws + ex.off_cu, CGDR_DT_INT64, {B + 1});
     const cgdrTensor ci = contiguous(ws + ex.off_ci, CGDR_DT_INT64, {NT, 2});
@@ -393,9 +485,38 @@ cgdrStatus cgdrChunkGatedDeltaRule(void* workspace, uint64_t workspaceSize, cgdr
                                            reinterpret_cast<int64_t*>(ws + ex.off_ci), status);
     if ((e = cudaGetLastError()) != cudaSuccess)
         return fail(CGDR_STATUS_CUDA_ERROR, "metadata kernel launch: %s", cudaGetErrorString(e));
+    auto blocks = [](int64_t n) { return static_cast<unsigned>(std::min<int64_t>((n + 255) / 256, 148 * 8)); };
+    if (padK) {
+        pad_heads_kernel<<<blocks(T * Nk * Dk), 256, 0, stream>>>(
+            static_cast<const __nv_bfloat16*>(ex.q.data), ex.q.strides[0], ex.q.strides[1], T, Nk, ex.Dk,
+            reinterpret_cast<__nv_bfloat16*>(ws + ex.off_qp), Dk);
+        pad_heads_kernel<<<blocks(T * Nk * Dk), 256, 0, stream>>>(
+            static_cast<const __nv_bfloat16*>(ex.k.data), ex.k.strides[0], ex.k.strides[1], T, Nk, ex.Dk,
+            reinterpret_cast<__nv_bfloat16*>(ws + ex.off_kp), Dk);
+    }
+    if (padV)
+        pad_heads_kernel<<<blocks(T * Nv * Dv), 256, 0, stream>>>(
+            static_cast<const __nv_bfloat16*>(ex.v.data), ex.v.strides[0], ex.v.strides[1], T, Nv, ex.Dv,
+            reinterpret_cast<__nv_bfloat16*>(ws + ex.off_vp), Dv);
+    if (padS)
+        pad_state_kernel<<<blocks(B * Nv * Dk * Dv), 256, 0, stream>>>(
+            ex.h0.data, ex.h0.dtype, ex.h0.strides[0], ex.h0.strides[1], ex.h0.strides[2], ex.h0.strides[3], B, Nv,
+            ex.Dv, ex.Dk, reinterpret_cast<float*>(ws + ex.off_h0p), Dk, Dv);
+    if ((e = cudaGetLastError()) != cudaSuccess)
+        return fail(CGDR_STATUS_CUDA_ERROR, "padding kernel launch: %s", cudaGetErrorString(e));
     if ((st = wy_enqueue(e_wy, status, stream))) return st;
     if ((st = fwd_h_enqueue(e_h, status, ws + ex.off_meta, stream))) return st;
     if ((st = chunk_o_enqueue(e_o, status, stream))) return st;
+    if (padV)
+        unpad_heads_kernel<<<blocks(T * Nv * ex.Dv), 256, 0, stream>>>(
+            reinterpret_cast<const __nv_bfloat16*>(ws + ex.off_op), Dv, T, Nv, ex.Dv,
+            static_cast<__nv_bfloat16*>(ex.out.data), ex.out.strides[0], ex.out.strides[1]);
+    if (padS)
+        unpad_state_kernel<<<blocks(B * Nv * ex.Dv * ex.Dk), 256, 0, stream>>>(
+            reinterpret_cast<const float*>(ws + ex.off_finp), Dk, Dv, B, Nv, ex.Dv, ex.Dk, ex.fin.data, ex.fin.dtype,
+            ex.fin.strides[0], ex.fin.strides[1], ex.fin.strides[2], ex.fin.strides[3]);
+    if ((e = cudaGetLastError()) != cudaSuccess)
+        return fail(CGDR_STATUS_CUDA_ERROR, "unpadding kernel launch: %s", cudaGetErrorString(e));
     return CGDR_STATUS_SUCCESS;
 }
 

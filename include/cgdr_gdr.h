@@ -24,9 +24,11 @@
  *     initialState, finalState [B, Nv, Dv, Dk]  bf16 or fp32
  *     actualSeqLengths [B]       int32, summing to T
  * with 0 < Nk, Nv <= 64, Nv % Nk == 0, 0 < Dk, Dv <= 128 and no empty
- * tensor.  This build computes Dk and Dv in {64, 128}; other values are
- * rejected with CGDR_STATUS_UNSUPPORTED.  query, key, value and out need
- * contiguous last dimensions and 16-byte multiple strides.
+ * tensor.  The kernels run at head widths 64 and 128; any other Dk or Dv is
+ * zero-padded to the next of the two in the workspace (exact: the padded
+ * columns stay zero through every product).  query, key, value and out need
+ * contiguous last dimensions, and 16-byte multiple strides where their width
+ * is 64 or 128.
  *
  * The recurrence runs with an fp32 state (the fla arithmetic); the output
  * passes the reference's own three-party accuracy check against its fp32

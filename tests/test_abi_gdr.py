@@ -51,6 +51,7 @@ def rejected(d, status):
     ("Dim128", (2, 64, 4, 4, 128, 128), {}),
     ("DifferentDKDV", (2, 64, 4, 4, 64, 128), {}),
     ("ScaleInvSqrt", (2, 64, 4, 4, 64, 64), {}),
+    ("MaxHeads48", (2, 64, 48, 48, 32, 32), {}),
 ])
 def test_accepts_the_reference_valid_cases(name, args, kw):
     op = plan(case(*args, **kw))
@@ -61,10 +62,18 @@ def test_accepts_the_reference_valid_cases(name, args, kw):
     assert op.workspace_size >= 2 * nt_max * nv * dk * dv + 2 * t * nv * (dk + 2 * dv) + 4 * t * nv
 
 
-def test_reference_valid_head_dim_outside_this_build():
-    """MaxHeads48 (dk = dv = 32) passes the reference's checks; this build
-    computes Dk, Dv in {64, 128} and says so."""
-    rejected(case(2, 64, 48, 48, 32, 32), "UNSUPPORTED")
+@pytest.mark.parametrize("dk,dv", [(32, 32), (96, 48), (128, 80), (1, 128)])
+def test_head_dims_outside_64_128_are_padded(dk, dv):
+    """MaxHeads48 (dk = dv = 32) and other widths the reference accepts run
+    through zero-padded copies at the next of 64 / 128; the workspace holds
+    them."""
+    bs, seq_len, nk, nv = 2, 64, 4, 8
+    op = plan(case(bs, seq_len, nk, nv, dk, dv))
+    t = bs * seq_len
+    kp, vp = (64 if dk <= 64 else 128), (64 if dv <= 64 else 128)
+    nt_max = (t + 63) // 64 + bs - 1
+    padded = 2 * 2 * t * nk * kp * (kp != dk) + 2 * 2 * t * nv * vp * (vp != dv) + 2 * 4 * bs * nv * kp * vp
+    assert op.workspace_size >= 2 * nt_max * nv * kp * vp + 2 * t * nv * (kp + 2 * vp) + padded
 
 
 @pytest.mark.parametrize("nk,nv", [(4, 3), (4, 5), (8, 7)])

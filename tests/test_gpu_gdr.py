@@ -76,6 +76,10 @@ def make_case(lens, nk, nv, dk, dv, state_dtype, seed, with_g=True):
     ([200, 64, 1000], 2, 4, 128, 128, torch.float32),
     ([1, 63, 65, 130], 1, 2, 64, 128, torch.bfloat16),
     ([512], 4, 4, 128, 64, torch.bfloat16),
+    # head widths outside {64, 128}: zero-padded copies in the workspace
+    ([100, 37], 2, 4, 32, 32, torch.float32),
+    ([150], 1, 2, 96, 48, torch.bfloat16),
+    ([64, 65], 2, 2, 128, 80, torch.float32),
 ])
 def test_operator_on_ragged_batches(lens, nk, nv, dk, dv, state):
     dev = _cuda()
