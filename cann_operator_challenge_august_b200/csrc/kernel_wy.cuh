@@ -513,35 +513,18 @@ __global__ void __launch_bounds__(608, 1) wy_tc_kernel(const __grid_constant__ W
             wy_group_bar(grp);
             // ---- blocks below the diagonal: B_im = T_ii A_im for the six pairs m < i,
             // then per diagonal d: T_ij = -sum_{m=j}^{i-1} B_im T_mj
-            // (thread: block pair of round q, row r, columns c4..c4+3)
-            const int r = (gt >> 2) & 15, c4 = 4 * (gt & 3), sub = gt >> 6;  // four blocks per round
-            if (ok) {
+            // (one warp per pair, thread rows r8 and r8 + 8, columns c4..c4+3)
+            const int r = (gt >> 2) & 15, c4 = 4 * (gt & 3), sub = gt >> 6;  // the steps' thread layout
+            if (ok && gw < 6) {
+                const int pidx = gw;  // pairs (1,0) (2,0) (2,1) (3,0) (3,1) (3,2)
+                const int bi = pidx == 0 ? 1 : (pidx < 3 ? 2 : 3);
+                const int bm = pidx == 0 ? 0 : (pidx < 3 ? pidx - 1 : pidx - 3);
+                const int r8 = lane >> 2, c4q = 4 * (lane & 3);
+                float4 y[2] = {};
+                wy_prod24(Tf + 16 * bi * LD + 16 * bi, LD, Am + 16 * bi * LD + 16 * bm, LD, r8, c4q, y);
 #pragma unroll
-                for (int q = 0; q < 2; ++q) {
-                    const int pidx = 4 * q + sub;  // pairs (1,0) (2,0) (2,1) (3,0) (3,1) (3,2)
-                    if (pidx >= 6) continue;
-                    const int bi = pidx == 0 ? 1 : (pidx < 3 ? 2 : 3);
-                    const int bm = pidx == 0 ? 0 : (pidx < 3 ? pidx - 1 : pidx - 3);
-                    const float4* trow = reinterpret_cast<const float4*>(Tf + (16 * bi + r) * LD + 16 * bi);
-                    float4 t4[4];
-#pragma unroll
-                    for (int k4 = 0; k4 < 4; ++k4) t4[k4] = trow[k4];
-                    // two partial sums (k < 8, k >= 8) halve the dependency chains
-                    float4 y[2] = {make_float4(0.0f, 0.0f, 0.0f, 0.0f), make_float4(0.0f, 0.0f, 0.0f, 0.0f)};
-#pragma unroll
-                    for (int k = 0; k < 16; ++k) {
-                        const float tk = k % 4 == 0 ? t4[k / 4].x : k % 4 == 1 ? t4[k / 4].y : k % 4 == 2 ? t4[k / 4].z
-                                                                                                          : t4[k / 4].w;
-                        const float4 a4 = *reinterpret_cast<const float4*>(Am + (16 * bi + k) * LD + 16 * bm + c4);
-                        float4& acc_ = y[k >> 3];
-                        acc_.x = fmaf(tk, a4.x, acc_.x);
-                        acc_.y = fmaf(tk, a4.y, acc_.y);
-                        acc_.z = fmaf(tk, a4.z, acc_.z);
-                        acc_.w = fmaf(tk, a4.w, acc_.w);
-                    }
-                    *reinterpret_cast<float4*>(Yb + pidx * 16 * Cfg::kLdY + r * Cfg::kLdY + c4) =
-                        make_float4(y[0].x + y[1].x, y[0].y + y[1].y, y[0].z + y[1].z, y[0].w + y[1].w);
-                }
+                for (int h = 0; h < 2; ++h)
+                    *reinterpret_cast<float4*>(Yb + pidx * 16 * Cfg::kLdY + (r8 + 8 * h) * Cfg::kLdY + c4q) = y[h];
             }
             wy_group_bar(grp);
             // ---- block forward substitution T_ij = -sum_{m=j}^{i-1} B_im T_mj in two
