@@ -9,7 +9,7 @@ H=32, K=V=128, chunk 64, h0 ~ 0.1 randn (fp32), final_state stored -- per
 rank, inputs generated on the device from seed + rank (weak scaling: the
 (sequence, head) pairs are independent, so every rank runs its own shard and
 there is no collective on the data path).  ``--config c5`` runs the
-BASELINE's multi-GPU config instead (B=8, T=8192, H=64, K=128, V=256) with
+the benchmark's multi-GPU config instead (B=8, T=8192, H=64, K=128, V=256) with
 its (b, h) pairs split evenly over the ranks (strong scaling).
 
 Metric: fwd_h tokens/s (tokens = B*T per call), whole job.  ``value`` is

@@ -1,4 +1,4 @@
-"""Shared test helpers: seeded inputs of the BASELINE configurations, layout
+"""Shared test helpers: seeded inputs of the benchmark configurations, layout
 adapters between the reference (head-major) and fla (token-major) layouts,
 and comparison statistics."""
 
@@ -85,7 +85,7 @@ def tm_to_hm_outputs(h, v):
     return np.ascontiguousarray(np.swapaxes(h, 1, 2)), np.ascontiguousarray(np.swapaxes(v, 1, 2))
 
 
-# ---- synthetic inputs of the BASELINE configurations --------------------------------
+# ---- synthetic inputs of the benchmark configurations -------------------------------
 
 def chunk_local_cumsum(x: torch.Tensor, seq_bounds) -> torch.Tensor:
     """Cumulative sum over T restarted at every 64-token chunk of every sequence.
@@ -101,7 +101,7 @@ def chunk_local_cumsum(x: torch.Tensor, seq_bounds) -> torch.Tensor:
 
 def make_inputs(B, T, H, K, V, *, HK=None, seed=0, dtype=torch.bfloat16, gate_shift=2.0, h0="randn",
                 cu_seqlens=None, device="cpu"):
-    """Seeded inputs in the fla layout, following the BASELINE recipes:
+    """Seeded inputs in the fla layout, following the benchmark recipes:
     k ~ randn L2-normalised over K; w = beta * k (beta = sigmoid(randn) per
     (t, h)); u ~ 0.5 randn; g = chunk-local cumsum of logsigmoid(randn +
     gate_shift); h0 ~ 0.1 randn (fp32), zeros, or None."""
@@ -134,7 +134,7 @@ def make_inputs(B, T, H, K, V, *, HK=None, seed=0, dtype=torch.bfloat16, gate_sh
 
 def varlen_lengths(n_seq, total, lo=64, hi=4096, seed=0):
     """Lengths uniform in [lo, hi], multiples of 64, rescaled to sum to `total`
-    (the varlen recipe of the BASELINE: 16 sequences packed into T_total)."""
+    (the benchmark's varlen recipe: 16 sequences packed into T_total)."""
     rng = np.random.default_rng(seed)
     lens = rng.integers(lo, hi + 1, size=n_seq)
     lens = np.maximum(64, (lens // 64) * 64)

@@ -8,7 +8,7 @@ Tolerances:
   fp32 summation order flipping a bf16 rounding of the bf16 state, which
   then propagates through slowly decaying chunks (the C oracle differs from
   the goldens the same way);
-* fp32-state numerics on the BASELINE recipes: rtol/atol 2e-2 against the
+* fp32-state numerics on the benchmark recipes: rtol/atol 2e-2 against the
   reference semantics (the north-star bar) and against the fp32-state oracle;
 * fp32 I/O: rtol/atol 1e-4 against the fp32-state oracle (fp64 sums).
 """
@@ -109,7 +109,7 @@ def test_golden_fp32_state_numerics(case):
         assert st["bad"] <= 0.01 * st["n"] and st["max_abs"] <= 0.125, f"{case}/{n}: {st}"
 
 
-# ---------------------------------------------------------------- BASELINE configs
+# ---------------------------------------------------------------- benchmark configs
 
 def _run_fla(inp, dev, **kw):
     t = {n: (x.to(dev) if isinstance(x, torch.Tensor) else x) for n, x in inp.items()}

@@ -79,7 +79,7 @@ def test_oracle_deterministic():
 
 
 def test_fp32_state_semantics_close_to_reference_on_baseline_recipe():
-    """On the BASELINE input recipe the Triton (fp32 state) arithmetic stays
+    """On the benchmark input recipe the Triton (fp32 state) arithmetic stays
     within the north-star 2e-2 of the reference rounding chain."""
     import torch
     inp = H.make_inputs(1, 1024, 4, 128, 128, seed=0)
