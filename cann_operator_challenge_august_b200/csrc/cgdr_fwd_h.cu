@@ -276,9 +276,11 @@ cgdrStatus build(const cgdrTensor* k, const cgdrTensor* w, const cgdrTensor* u, 
     if (tc_ok) {
         int vt = opt.v_tile;
         if (vt == 0) {
-            // Widest tile that still gives at least one CTA per SM; 64-column
-            // tiles run two CTAs per SM.
-            vt = (d.V % 128 == 0 && d.N * d.HV * (d.V / 128) >= 148) ? 128 : 64;
+            // 64-column tiles while they fit one CTA per SM (the shortest chain);
+            // beyond that 128-column tiles, one CTA per SM: on B=4, T=8192, H=32,
+            // K=V=128 (256 64-column tasks) they take 0.288 ms against 0.307 ms
+            // for two 64-column CTAs per SM.
+            vt = (d.V % 128 == 0 && d.N * d.HV * (d.V / 64) > 148) ? 128 : 64;
         }
         if (vt != 64 && vt != 128) {
             delete ex_;
