@@ -360,6 +360,8 @@ def main() -> int:
     ap.add_argument("--config", choices=sorted(CONFIGS), default="ns")
     ap.add_argument("--numerics", choices=["fp32_state", "reference"], default="fp32_state")
     ap.add_argument("--v-tile", type=int, default=0)
+    ap.add_argument("--gdr-path", choices=["auto", "fused", "three_kernels"], default="auto",
+                    help="--op gdr: the recurrence and output kernels (default: the planner's choice)")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--op", choices=["fwd_h", "chunk_o", "wy", "gdr"], default="fwd_h",
@@ -857,13 +859,15 @@ def main_gdr(args) -> int:
     asl = torch.full((B,), T, dtype=torch.int32, device=dev)
     out = torch.empty_like(v)
     fin = torch.empty_like(h0)
-    op0 = cg.ChunkGatedDeltaRule(q, k, v, beta, h0, asl, g, None, out, fin)
+    gpath = args.gdr_path
+    op0 = cg.ChunkGatedDeltaRule(q, k, v, beta, h0, asl, g, None, out, fin, path=gpath)
     ws = torch.empty(op0.workspace_size, dtype=torch.uint8, device=dev)
+    path_taken = op0.path
     del op0
     stream = torch.cuda.current_stream(dev)
 
     def step():
-        cg.ChunkGatedDeltaRule(q, k, v, beta, h0, asl, g, None, out, fin)(ws)
+        cg.ChunkGatedDeltaRule(q, k, v, beta, h0, asl, g, None, out, fin, path=gpath)(ws)
 
     for _ in range(args.warmup):
         step()
@@ -904,7 +908,7 @@ def main_gdr(args) -> int:
 
     def e2e_step():
         d = [t.to(dev, non_blocking=True) for t in host]
-        o, f = cg.chunk_gated_delta_rule(d[0], d[1], d[2], d[3], d[4], d[5], None, d[6], workspace=ws)
+        o, f = cg.chunk_gated_delta_rule(d[0], d[1], d[2], d[3], d[4], d[5], None, d[6], workspace=ws, path=gpath)
         host_out[0].copy_(o, non_blocking=True)
         host_out[1].copy_(f, non_blocking=True)
 
@@ -954,15 +958,19 @@ def main_gdr(args) -> int:
             "config": dict(config_block(args.config, c, world, nbytes),
                            workload=f"{args.config}: chunked Gated DeltaNet forward (WY, recurrence, chunk output) bf16, "
                                     f"{B} sequences of T={T} packed as TND, Nk={HK} Nv={H} Dk={K} Dv={V}, "
-                                    f"fp32 initial/final state"),
-            "gpu_launches": 4 * args.steps,
+                                    f"fp32 initial/final state",
+                           path=path_taken),
+            # per call: metadata, WY, the recurrence's sequence order, then the fused kernel
+            # or the recurrence and the chunk output
+            "gpu_launches": (4 if path_taken == "fused" else 5) * args.steps,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                          else "fallback",
                          "algorithmic_bytes_per_launch": nbytes, "launch_ms": per_launch_ms,
-                         "bytes_basis": "operator inputs and outputs only (the intermediates of the three kernels "
-                                        "are not counted)",
-                         "traffic": None, "kernel": "wy+fwd_h+chunk_o"},
+                         "bytes_basis": "operator inputs and outputs only (intermediates between kernels are "
+                                        "not counted)",
+                         "traffic": None,
+                         "kernel": "wy+fwd_ho" if path_taken == "fused" else "wy+fwd_h+chunk_o"},
             "clocks": clk,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": e2e_ms},

@@ -60,6 +60,8 @@ EXPORTS_BY_HEADER = {
     "cgdr_varlen.h": ("cgdrPrepareChunkIndices",),
     "cgdr_gdr.h": (
         "cgdrChunkGatedDeltaRuleGetWorkspaceSize",
+        "cgdrChunkGatedDeltaRuleGetWorkspaceSizeEx",
+        "cgdrGetGdrPath",
         "cgdrChunkGatedDeltaRule",
         "cgdrDestroyGdrExecutor",
     ),
@@ -96,6 +98,13 @@ class CgdrChunkOOptions(ctypes.Structure):
 
 class CgdrWyOptions(ctypes.Structure):
     _fields_ = [("wait_timeout_ms", ctypes.c_int32), ("reserved", ctypes.c_int32 * 7)]
+
+
+class CgdrGdrOptions(ctypes.Structure):
+    _fields_ = [("path", ctypes.c_int32), ("reserved", ctypes.c_int32 * 7)]
+
+
+GDR_PATHS = {"auto": 0, "fused": 1, "three_kernels": 2}
 
 
 class CgdrFwdHPlan(ctypes.Structure):
@@ -164,6 +173,11 @@ def load() -> ctypes.CDLL:
     lib.cgdrDestroyWyExecutor.restype = None
     lib.cgdrChunkGatedDeltaRuleGetWorkspaceSize.argtypes = [T] * 7 + [ctypes.c_float, T, T, u64p, exp]
     lib.cgdrChunkGatedDeltaRuleGetWorkspaceSize.restype = ctypes.c_int
+    lib.cgdrChunkGatedDeltaRuleGetWorkspaceSizeEx.argtypes = (
+        [T] * 7 + [ctypes.c_float, T, T, ctypes.POINTER(CgdrGdrOptions), u64p, exp])
+    lib.cgdrChunkGatedDeltaRuleGetWorkspaceSizeEx.restype = ctypes.c_int
+    lib.cgdrGetGdrPath.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int32)]
+    lib.cgdrGetGdrPath.restype = ctypes.c_int
     lib.cgdrChunkGatedDeltaRule.argtypes = [ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p, ctypes.c_void_p]
     lib.cgdrChunkGatedDeltaRule.restype = ctypes.c_int
     lib.cgdrDestroyGdrExecutor.argtypes = [ctypes.c_void_p]

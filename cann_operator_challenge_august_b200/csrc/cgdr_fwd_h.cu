@@ -15,6 +15,7 @@
 #include "host_stages.cuh"
 #include "host_util.cuh"
 #include "kernel_simt.cuh"
+#include "kernel_ho.cuh"
 #include "kernel_tc.cuh"
 
 using namespace cgdr;
@@ -505,6 +506,94 @@ cgdrStatus fwd_h_enqueue(const cgdrExecutor* executor, int* status, uint8_t* met
         if ((e = cudaGetLastError()) != cudaSuccess)
             return fail(CGDR_STATUS_CUDA_ERROR, "general kernel launch: %s", cudaGetErrorString(e));
     }
+    return CGDR_STATUS_SUCCESS;
+}
+
+bool fwd_ho_applies(const cgdrExecutor* ex)
+{
+    const FwdHParams& p = ex->p;
+    return p.K == 128 && (p.V == 64 || p.V == 128) && p.numerics == 1 && p.io_dtype == kBF16 &&
+           ex->plan.layout == CGDR_LAYOUT_TOKEN_MAJOR;
+}
+
+cgdrStatus fwd_ho_enqueue(const cgdrExecutor* executor, const cgdrTensor* q, const cgdrTensor* o, float scale,
+                          int* status, uint8_t* meta, cudaStream_t stream)
+{
+    if (!fwd_ho_applies(executor))
+        return fail(CGDR_STATUS_UNSUPPORTED, "internal: the fused recurrence + output kernel does not cover this plan");
+    FwdHParams p = executor->p;
+    p.status = status;
+    p.h = nullptr;
+    p.v_new = nullptr;
+    // q [B, T, HK, K] and o [B, T, H, V], token-major like k and u
+    if (q->ndim != 4 || o->ndim != 4 || q->strides[3] != 1 || o->strides[3] != 1 || q->shape[3] != p.K ||
+        o->shape[3] != p.V || q->shape[2] != p.HK || o->shape[2] != p.H || q->shape[1] != p.T || o->shape[1] != p.T ||
+        q->shape[0] != p.B || o->shape[0] != p.B || q->dtype != CGDR_DT_BF16 || o->dtype != CGDR_DT_BF16)
+        return fail(CGDR_STATUS_UNSUPPORTED, "internal: q / o views do not match the recurrence plan");
+    if ((reinterpret_cast<uintptr_t>(o->data) & 15) || (o->strides[1] % 8) || (o->strides[2] % 8) || (o->strides[0] % 8))
+        return fail(CGDR_STATUS_BAD_STRIDE, "out needs 16-byte aligned rows for the fused kernel");
+    cudaError_t e = cudaSuccess;
+    if (p.varlen) {
+        int32_t* base = reinterpret_cast<int32_t*>(meta);
+        int32_t* order = reinterpret_cast<int32_t*>(meta + align256(4 * static_cast<uint64_t>(p.N + 1)));
+        p.seq_chunk_base = base;
+        p.seq_order = order;
+        varlen_prep_kernel<<<1, 1024, 0, stream>>>(p.cu_seqlens, p.N, p.T, p.NT, base, order, p.status);
+        if ((e = cudaGetLastError()) != cudaSuccess)
+            return fail(CGDR_STATUS_CUDA_ERROR, "varlen metadata kernel: %s", cudaGetErrorString(e));
+    }
+    const int64_t grid = p.N * p.H;
+    if (grid == 0) return CGDR_STATUS_SUCCESS;
+    HoArgs args;
+    memset(&args, 0, sizeof(args));
+    cgdrStatus st;
+    {
+        const int64_t size[4] = {p.K, p.HK, p.T, p.B}, stride[4] = {1, p.k_sh, p.k_st, p.k_sb};
+        const uint32_t box[4] = {64, 1, 64, 1};
+        if ((st = make_map(&args.maps.k, const_cast<void*>(p.k), 4, size, stride, box, "k"))) return st;
+    }
+    {
+        const int64_t size[4] = {p.K, p.H, p.T, p.B}, stride[4] = {1, p.w_sh, p.w_st, p.w_sb};
+        const uint32_t box[4] = {64, 1, 16, 1};
+        if ((st = make_map(&args.maps.w, const_cast<void*>(p.w), 4, size, stride, box, "w"))) return st;
+    }
+    {
+        const int64_t size[4] = {p.K, p.HK, p.T, p.B}, stride[4] = {1, q->strides[2], q->strides[1], q->strides[0]};
+        const uint32_t box[4] = {64, 1, 16, 1};
+        if ((st = make_map(&args.maps.q, q->data, 4, size, stride, box, "q"))) return st;
+    }
+    {
+        const int64_t size[4] = {p.V, p.H, p.T, p.B}, stride[4] = {1, p.u_sh, p.u_st, p.u_sb};
+        const uint32_t box[4] = {64, 1, 64, 1};
+        if ((st = make_map(&args.maps.u, const_cast<void*>(p.u), 4, size, stride, box, "u"))) return st;
+    }
+    {
+        const int64_t size[4] = {p.V, p.H, p.T, p.B}, stride[4] = {1, o->strides[2], o->strides[1], o->strides[0]};
+        const uint32_t box[4] = {64, 1, 16, 1};
+        if ((st = make_map(&args.maps.o, o->data, 4, size, stride, box, "o"))) return st;
+    }
+    args.p = p;
+    args.x.o = static_cast<__nv_bfloat16*>(o->data);
+    args.x.o_sb = o->strides[0];
+    args.x.o_st = o->strides[1];
+    args.x.o_sh = o->strides[2];
+    args.x.scale = scale;
+    if (p.V == 128) {
+        using Cfg = HoConfig<128>;
+        e = cudaFuncSetAttribute(fwd_ho_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+        if (e == cudaSuccess) {
+            fwd_ho_tc_kernel<128><<<static_cast<unsigned>(grid), Cfg::kThreads, Cfg::kSmemBytes, stream>>>(args);
+            e = cudaGetLastError();
+        }
+    } else {
+        using Cfg = HoConfig<64>;
+        e = cudaFuncSetAttribute(fwd_ho_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+        if (e == cudaSuccess) {
+            fwd_ho_tc_kernel<64><<<static_cast<unsigned>(grid), Cfg::kThreads, Cfg::kSmemBytes, stream>>>(args);
+            e = cudaGetLastError();
+        }
+    }
+    if (e != cudaSuccess) return fail(CGDR_STATUS_CUDA_ERROR, "fused recurrence + output kernel launch: %s", cudaGetErrorString(e));
     return CGDR_STATUS_SUCCESS;
 }
 

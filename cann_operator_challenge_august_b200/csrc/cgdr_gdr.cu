@@ -193,6 +193,7 @@ struct cgdrGdrExecutor {
     float scale;
     int64_t B, T, Nk, Nv, Dk, Dv, nt_max;
     int64_t Kp, Vp;  // head widths the kernels run at (Dk, Dv padded up to 64 or 128)
+    bool fused;      // recurrence and chunk output in one kernel (no h / v_new in the workspace)
     // workspace layout (byte offsets)
     uint64_t off_cu, off_cb, off_ci, off_meta, off_gc, off_w, off_u, off_vn, off_h, total;
     uint64_t off_qp, off_kp, off_vp, off_op, off_h0p, off_finp;  // padding buffers (Kp != Dk or Vp != Dv)
@@ -247,8 +248,12 @@ bool sixteen(const cgdrTensor* t)
 
 cgdrStatus build_gdr(const cgdrTensor* q, const cgdrTensor* k, const cgdrTensor* v, const cgdrTensor* beta,
                      const cgdrTensor* h0, const cgdrTensor* asl, const cgdrTensor* g, float scale,
-                     const cgdrTensor* out, const cgdrTensor* fin, uint64_t* ws_size, cgdrGdrExecutor** exo)
+                     const cgdrTensor* out, const cgdrTensor* fin, const cgdrGdrOptions* options, uint64_t* ws_size,
+                     cgdrGdrExecutor** exo)
 {
+    const int32_t path = options ? options->path : CGDR_GDR_PATH_AUTO;
+    if (path != CGDR_GDR_PATH_AUTO && path != CGDR_GDR_PATH_FUSED && path != CGDR_GDR_PATH_THREE_KERNELS)
+        return fail(CGDR_STATUS_UNSUPPORTED, "unknown path %d", static_cast<int>(path));
     if (!ws_size || !exo) return fail(CGDR_STATUS_NULL_ARGUMENT, "workspaceSize and executor must not be NULL");
     *exo = nullptr;
     // aclnn_chunk_gated_delta_rule.cpp:64-76: every tensor but g is required
@@ -328,6 +333,15 @@ cgdrStatus build_gdr(const cgdrTensor* q, const cgdrTensor* k, const cgdrTensor*
     ex->B = B; ex->T = T; ex->Nk = Nk; ex->Nv = Nv; ex->Dk = Dk; ex->Dv = Dv;
     ex->Kp = Kp; ex->Vp = Vp;
     ex->nt_max = (T + kChunk - 1) / kChunk + B - 1;
+    // the fused kernel runs K = 128 (Dk in (64, 128]); AUTO takes it once the
+    // (sequence, head) tasks fill half the SMs, below which the separate
+    // recurrence (64-column tiles) and the chunk-parallel output spread wider
+    const bool fused_applies = Kp == 128;
+    if (path == CGDR_GDR_PATH_FUSED && !fused_applies) {
+        delete ex;
+        return fail(CGDR_STATUS_UNSUPPORTED, "the fused path needs 64 < Dk <= 128, got Dk=%lld", (long long)Dk);
+    }
+    ex->fused = path == CGDR_GDR_PATH_FUSED || (path == CGDR_GDR_PATH_AUTO && fused_applies && B * Nv >= 74);
     uint64_t off = kHeader;
     auto take = [&](uint64_t bytes) {
         const uint64_t at = off;
@@ -342,8 +356,11 @@ cgdrStatus build_gdr(const cgdrTensor* q, const cgdrTensor* k, const cgdrTensor*
     ex->off_gc = take(4 * static_cast<uint64_t>(T * Nv));
     ex->off_w = take(2 * static_cast<uint64_t>(T * Nv * Kp));
     ex->off_u = take(2 * static_cast<uint64_t>(T * Nv * Vp));
-    ex->off_vn = take(2 * static_cast<uint64_t>(T * Nv * Vp));
-    ex->off_h = take(2 * static_cast<uint64_t>(ex->nt_max * Nv * Kp * Vp));
+    ex->off_vn = ex->off_h = 0;
+    if (!ex->fused) {
+        ex->off_vn = take(2 * static_cast<uint64_t>(T * Nv * Vp));
+        ex->off_h = take(2 * static_cast<uint64_t>(ex->nt_max * Nv * Kp * Vp));
+    }
     ex->off_qp = ex->off_kp = ex->off_vp = ex->off_op = ex->off_h0p = ex->off_finp = 0;
     if (padK) {
         ex->off_qp = take(2 * static_cast<uint64_t>(T * Nk * Kp));
@@ -376,7 +393,27 @@ cgdrStatus cgdrChunkGatedDeltaRuleGetWorkspaceSize(const cgdrTensor* query, cons
                                                    uint64_t* workspaceSize, cgdrGdrExecutor** executor)
 {
     return build_gdr(query, key, value, beta, initialState, actualSeqLengths, gOptional, scaleValue, out, finalState,
-                     workspaceSize, executor);
+                     nullptr, workspaceSize, executor);
+}
+
+cgdrStatus cgdrChunkGatedDeltaRuleGetWorkspaceSizeEx(const cgdrTensor* query, const cgdrTensor* key,
+                                                     const cgdrTensor* value, const cgdrTensor* beta,
+                                                     const cgdrTensor* initialState,
+                                                     const cgdrTensor* actualSeqLengths, const cgdrTensor* gOptional,
+                                                     float scaleValue, const cgdrTensor* out,
+                                                     const cgdrTensor* finalState, const cgdrGdrOptions* options,
+                                                     uint64_t* workspaceSize, cgdrGdrExecutor** executor)
+{
+    return build_gdr(query, key, value, beta, initialState, actualSeqLengths, gOptional, scaleValue, out, finalState,
+                     options, workspaceSize, executor);
+}
+
+cgdrStatus cgdrGetGdrPath(const cgdrGdrExecutor* executor, int32_t* path)
+{
+    if (!executor || executor->magic != kMagicGdr) return fail(CGDR_STATUS_BAD_EXECUTOR, "invalid executor");
+    if (!path) return fail(CGDR_STATUS_NULL_ARGUMENT, "path must not be NULL");
+    *path = executor->fused ? CGDR_GDR_PATH_FUSED : CGDR_GDR_PATH_THREE_KERNELS;
+    return CGDR_STATUS_SUCCESS;
 }
 
 void cgdrDestroyGdrExecutor(cgdrGdrExecutor* executor)
@@ -440,6 +477,8 @@ cgdrStatus cgdrChunkGatedDeltaRule(void* workspace, uint64_t workspaceSize, cgdr
     const cgdrTensor gc = contiguous(ws + ex.off_gc, CGDR_DT_FLOAT32, {1, T, Nv});
     const cgdrTensor w = contiguous(ws + ex.off_w, CGDR_DT_BF16, {1, T, Nv, Dk});
     const cgdrTensor u = contiguous(ws + ex.off_u, CGDR_DT_BF16, {1, T, Nv, Dv});
+    // on the fused path h and v_new have no buffer: the recurrence plan gets a
+    // placeholder h view (shape checks only; nothing reads or writes it) and no v_new
     const cgdrTensor vn = contiguous(ws + ex.off_vn, CGDR_DT_BF16, {1, T, Nv, Dv});
     const cgdrTensor h = contiguous(ws + ex.off_h, CGDR_DT_BF16, {1, NT, Nv, Dk, Dv});
 
@@ -467,13 +506,14 @@ cgdrStatus cgdrChunkGatedDeltaRule(void* workspace, uint64_t workspaceSize, cgdr
     memset(&opt, 0, sizeof(opt));
     opt.layout = CGDR_LAYOUT_TOKEN_MAJOR;
     opt.numerics = CGDR_NUMERICS_FP32_STATE;
-    if ((st = cgdrChunkGatedDeltaRuleFwdHGetWorkspaceSizeEx(&k4, &w, &u, &gc, &h0, &cu, &ci, nullptr, kChunk, &h, &vn,
-                                                            &fin, &opt, &sz, &e_h)))
+    if ((st = cgdrChunkGatedDeltaRuleFwdHGetWorkspaceSizeEx(&k4, &w, &u, &gc, &h0, &cu, &ci, nullptr, kChunk, &h,
+                                                            ex.fused ? nullptr : &vn, &fin, &opt, &sz, &e_h)))
         return st;
+    if (ex.fused && !fwd_ho_applies(e_h)) return fail(CGDR_STATUS_UNSUPPORTED, "internal: fused plan not applicable");
     if (fwd_h_meta_bytes(e_h) > align256(4 * static_cast<uint64_t>(B + 1)) + align256(4 * static_cast<uint64_t>(B)))
         return fail(CGDR_STATUS_UNSUPPORTED, "internal: recurrence metadata does not fit");
-    if ((st = cgdrChunkGatedDeltaRuleFwdOGetWorkspaceSize(&q4, &k4, &vn, &h, &gc, &cu, &ci, ex.scale, kChunk, &o4,
-                                                          nullptr, &sz, &e_o)))
+    if (!ex.fused && (st = cgdrChunkGatedDeltaRuleFwdOGetWorkspaceSize(&q4, &k4, &vn, &h, &gc, &cu, &ci, ex.scale,
+                                                                       kChunk, &o4, nullptr, &sz, &e_o)))
         return st;
 
     // enqueue: status word, metadata, WY, recurrence, chunk output (one stream)
@@ -505,8 +545,12 @@ cgdrStatus cgdrChunkGatedDeltaRule(void* workspace, uint64_t workspaceSize, cgdr
     if ((e = cudaGetLastError()) != cudaSuccess)
         return fail(CGDR_STATUS_CUDA_ERROR, "padding kernel launch: %s", cudaGetErrorString(e));
     if ((st = wy_enqueue(e_wy, status, stream))) return st;
-    if ((st = fwd_h_enqueue(e_h, status, ws + ex.off_meta, stream))) return st;
-    if ((st = chunk_o_enqueue(e_o, status, stream))) return st;
+    if (ex.fused) {
+        if ((st = fwd_ho_enqueue(e_h, &q4, &o4, ex.scale, status, ws + ex.off_meta, stream))) return st;
+    } else {
+        if ((st = fwd_h_enqueue(e_h, status, ws + ex.off_meta, stream))) return st;
+        if ((st = chunk_o_enqueue(e_o, status, stream))) return st;
+    }
     if (padV)
         unpad_heads_kernel<<<blocks(T * Nv * ex.Dv), 256, 0, stream>>>(
             reinterpret_cast<const __nv_bfloat16*>(ws + ex.off_op), Dv, T, Nv, ex.Dv,

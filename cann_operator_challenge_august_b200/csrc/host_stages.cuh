@@ -20,6 +20,13 @@ uint64_t fwd_h_meta_bytes(const cgdrExecutor* ex);
 cgdrStatus fwd_h_enqueue(const cgdrExecutor* ex, int* status, uint8_t* meta, cudaStream_t stream);
 cgdrStatus chunk_o_enqueue(const cgdrChunkOExecutor* ex, int* status, cudaStream_t stream);
 cgdrStatus wy_enqueue(const cgdrWyExecutor* ex, int* status, cudaStream_t stream);
+// The recurrence and the chunk output in one kernel (kernel_ho.cuh), for a
+// recurrence plan with K = 128, V in {64, 128}, fp32 state, token-major bf16.
+// q [B, T, HK, K] and o [B, T, H, V] are bf16 views with a unit inner stride;
+// the plan's h and v_new are neither read nor written.
+bool fwd_ho_applies(const cgdrExecutor* ex);
+cgdrStatus fwd_ho_enqueue(const cgdrExecutor* ex, const cgdrTensor* q, const cgdrTensor* o, float scale, int* status,
+                          uint8_t* meta, cudaStream_t stream);
 
 }  // namespace host
 }  // namespace cgdr

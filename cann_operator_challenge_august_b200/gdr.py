@@ -188,20 +188,35 @@ class ChunkGatedDeltaRule:
     initial_state, actual_seq_lengths, g, scale, out, final_state)``
     validates (the reference's checks) and sizes the workspace;
     ``op(workspace)`` enqueues the metadata, WY, recurrence and chunk-output
-    kernels on the current stream."""
+    kernels on the current stream.  ``path`` selects the recurrence and
+    output kernels: ``"fused"`` (one kernel; h and v_new stay on chip),
+    ``"three_kernels"`` (recurrence then chunk output) or ``"auto"``."""
 
-    def __init__(self, query, key, value, beta, initial_state, actual_seq_lengths, g, scale, out, final_state):
+    def __init__(self, query, key, value, beta, initial_state, actual_seq_lengths, g, scale, out, final_state,
+                 *, path: str = "auto"):
         lib = _lib.load()
         self._keep = (query, key, value, beta, initial_state, actual_seq_lengths, g, out, final_state)
         ws = ctypes.c_uint64(0)
         ex = ctypes.c_void_p(None)
         descs = [_desc(x) for x in (query, key, value, beta, initial_state, actual_seq_lengths, g)]
-        st = lib.cgdrChunkGatedDeltaRuleGetWorkspaceSize(
+        if path not in _lib.GDR_PATHS:
+            raise ValueError(f"path must be one of {sorted(_lib.GDR_PATHS)}")
+        opt = _lib.CgdrGdrOptions(path=_lib.GDR_PATHS[path])
+        st = lib.cgdrChunkGatedDeltaRuleGetWorkspaceSizeEx(
             *[ctypes.byref(d) for d in descs], float(scale if scale is not None else 0.0), ctypes.byref(_desc(out)),
-            ctypes.byref(_desc(final_state)), ctypes.byref(ws), ctypes.byref(ex))
-        _lib.check(st, "cgdrChunkGatedDeltaRuleGetWorkspaceSize")
+            ctypes.byref(_desc(final_state)), ctypes.byref(opt), ctypes.byref(ws), ctypes.byref(ex))
+        _lib.check(st, "cgdrChunkGatedDeltaRuleGetWorkspaceSizeEx")
         self._ex = ex
         self.workspace_size = int(ws.value)
+
+    @property
+    def path(self) -> str:
+        """``"fused"`` or ``"three_kernels"``: the kernels this plan runs."""
+        if self._ex is None:
+            raise RuntimeError("executor already consumed")
+        out = ctypes.c_int32(0)
+        _lib.check(_lib.load().cgdrGetGdrPath(self._ex, ctypes.byref(out)), "cgdrGetGdrPath")
+        return {v: k for k, v in _lib.GDR_PATHS.items()}[int(out.value)]
 
     def __call__(self, workspace: torch.Tensor, stream: int | None = None) -> None:
         if self._ex is None:
@@ -232,6 +247,7 @@ def chunk_gated_delta_rule(
     *,
     workspace: torch.Tensor | None = None,
     check_device_status: bool = False,
+    path: str = "auto",
 ) -> tuple[torch.Tensor, torch.Tensor]:
     """The reference operator's Python form (torch_npu.npu_chunk_gated_delta_rule):
     query, key ``[T, Nk, Dk]``, value ``[T, Nv, Dv]``, beta ``[T, Nv]`` (bf16),
@@ -239,11 +255,13 @@ def chunk_gated_delta_rule(
     ``[B]`` int32 (summing to T), scale (default ``Dk ** -0.5``), g ``[T, Nv]``
     fp32 per-token log gate (optional).  Returns ``out [T, Nv, Dv]`` (bf16)
     and ``final_state`` (the dtype of initial_state).  ``workspace`` may be a
-    caller-owned uint8 buffer of at least the planned size."""
+    caller-owned uint8 buffer of at least the planned size.  ``path``: see
+    :class:`ChunkGatedDeltaRule`."""
     _require_cuda(query, key, value, beta, initial_state, actual_seq_lengths, g)
     out = torch.empty_like(value)
     final_state = torch.empty_like(initial_state)
-    op = ChunkGatedDeltaRule(query, key, value, beta, initial_state, actual_seq_lengths, g, scale, out, final_state)
+    op = ChunkGatedDeltaRule(query, key, value, beta, initial_state, actual_seq_lengths, g, scale, out, final_state,
+                             path=path)
     if workspace is None or workspace.numel() * workspace.element_size() < op.workspace_size:
         workspace = torch.empty(max(op.workspace_size, 256), dtype=torch.uint8, device=value.device)
     op(workspace)

@@ -1,8 +1,9 @@
 /*
  * cgdr_gdr.h -- C ABI of the chunked Gated DeltaNet forward operator on B200
- * (sm_100a), composed of this library's three kernels: the WY representation
- * (cgdr_wy.h), the hidden-state recurrence (cgdr_fwd_h.h) and the chunk
- * output (cgdr_chunk_o.h).
+ * (sm_100a), composed of this library's kernels: the WY representation
+ * (cgdr_wy.h), then either the hidden-state recurrence (cgdr_fwd_h.h)
+ * followed by the chunk output (cgdr_chunk_o.h), or one kernel that does
+ * both.
  *
  * It is the drop-in counterpart of the reference's full operator
  * aclnnChunkGatedDeltaRule (ref/chunk_gated_delta_rule/op_host/op_api/
@@ -34,9 +35,9 @@
  * passes the reference's own three-party accuracy check against its fp32
  * golden (ref/chunk_gated_delta_rule/tests/assets/impl/compare.py).
  * The workspace holds the intermediate tensors (chunk-local cumulative
- * gate, w, u, v_new, the per-chunk states h) and the varlen metadata that a
- * device kernel derives from actualSeqLengths, so phase 2 needs no host
- * synchronisation.
+ * gate, w, u; on the three-kernel path also v_new and the per-chunk states
+ * h) and the varlen metadata that a device kernel derives from
+ * actualSeqLengths, so phase 2 needs no host synchronisation.
  */
 #ifndef CGDR_GDR_H_
 #define CGDR_GDR_H_
@@ -55,6 +56,37 @@ cgdrStatus cgdrChunkGatedDeltaRuleGetWorkspaceSize(
     const cgdrTensor* initialState, const cgdrTensor* actualSeqLengths, const cgdrTensor* gOptional,
     float scaleValue, const cgdrTensor* out, const cgdrTensor* finalState, uint64_t* workspaceSize,
     cgdrGdrExecutor** executor);
+
+/* Which kernels phase 2 runs after the WY kernel:
+ *   FUSED          one kernel for the recurrence and the chunk output; the
+ *                  per-chunk states h and v_new stay on chip (Dk padded to
+ *                  128, i.e. 64 < Dk <= 128);
+ *   THREE_KERNELS  the recurrence (h and v_new to the workspace), then the
+ *                  chunk output;
+ *   AUTO           FUSED where it applies and B * Nv >= 74 (half the SMs of
+ *                  a B200 hold one (sequence, head) task each), else
+ *                  THREE_KERNELS. */
+typedef enum {
+    CGDR_GDR_PATH_AUTO = 0,
+    CGDR_GDR_PATH_FUSED = 1,
+    CGDR_GDR_PATH_THREE_KERNELS = 2
+} cgdrGdrPath;
+
+typedef struct {
+    int32_t path;         /* cgdrGdrPath */
+    int32_t reserved[7];  /* zero */
+} cgdrGdrOptions;
+
+/* Phase 1 with options (NULL: all defaults).  CGDR_GDR_PATH_FUSED for a
+ * shape it does not cover returns CGDR_STATUS_UNSUPPORTED. */
+cgdrStatus cgdrChunkGatedDeltaRuleGetWorkspaceSizeEx(
+    const cgdrTensor* query, const cgdrTensor* key, const cgdrTensor* value, const cgdrTensor* beta,
+    const cgdrTensor* initialState, const cgdrTensor* actualSeqLengths, const cgdrTensor* gOptional,
+    float scaleValue, const cgdrTensor* out, const cgdrTensor* finalState, const cgdrGdrOptions* options,
+    uint64_t* workspaceSize, cgdrGdrExecutor** executor);
+
+/* The path a plan takes (CGDR_GDR_PATH_FUSED or CGDR_GDR_PATH_THREE_KERNELS). */
+cgdrStatus cgdrGetGdrPath(const cgdrGdrExecutor* executor, int32_t* path);
 
 /* Phase 2: enqueue on `stream`; consumes `executor`.  The first 256 bytes of
  * the workspace hold the device status word (cgdrReadDeviceStatus): bit 0x2

@@ -124,3 +124,48 @@ def test_requires_every_tensor_but_g():
     d = case(2, 64, 4, 8, 64, 64)
     d["beta"] = None
     rejected(d, "NULL_ARGUMENT")
+
+
+# ---------------------------------------------------------------- recurrence + output path
+
+def plan_path(d, path):
+    return cg.ChunkGatedDeltaRule(d["query"], d["key"], d["value"], d["beta"], d["initial_state"],
+                                  d["actual_seq_lengths"], d["g"], d["scale"], d["out"], d["final_state"], path=path)
+
+
+@pytest.mark.parametrize("args,expected", [
+    ((8, 64, 4, 16, 128, 128), "fused"),          # B * Nv = 128 >= 74, Dk = 128
+    ((2, 64, 16, 64, 96, 64), "fused"),           # Dk 96 runs padded to 128
+    ((2, 64, 4, 8, 128, 128), "three_kernels"),   # B * Nv = 16: too few tasks
+    ((8, 64, 4, 16, 64, 128), "three_kernels"),   # Dk = 64: the fused kernel runs K = 128 only
+])
+def test_auto_path(args, expected):
+    assert plan_path(case(*args), "auto").path == expected
+
+
+def test_fused_workspace_has_no_states():
+    """The fused plan keeps h and v_new on chip: its workspace is smaller than
+    the three-kernel plan's by the per-chunk states and v_new."""
+    bs, seq_len, nk, nv, dk, dv = 8, 64, 4, 16, 128, 128
+    d = case(bs, seq_len, nk, nv, dk, dv)
+    fused, three = plan_path(d, "fused"), plan_path(d, "three_kernels")
+    assert (fused.path, three.path) == ("fused", "three_kernels")
+    t = bs * seq_len
+    nt_max = (t + 63) // 64 + bs - 1
+    assert fused.workspace_size < 2 * nt_max * nv * dk * dv
+    assert three.workspace_size - fused.workspace_size >= 2 * nt_max * nv * dk * dv + 2 * t * nv * dv
+
+
+def test_forced_fused_path_on_small_batches():
+    assert plan_path(case(1, 64, 4, 4, 128, 64), "fused").path == "fused"
+
+
+def test_fused_path_rejects_dk_64():
+    with pytest.raises(cg.CgdrError) as ei:
+        plan_path(case(2, 64, 4, 4, 64, 64), "fused")
+    assert ei.value.status_name == "UNSUPPORTED"
+
+
+def test_unknown_path_name():
+    with pytest.raises(ValueError):
+        plan_path(case(2, 64, 4, 4, 64, 64), "two_kernels")

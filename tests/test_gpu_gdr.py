@@ -43,17 +43,28 @@ def check(out, fin, golden_out, golden_fin, bench_out, bench_fin):
     assert r["pass"], ("final_state", r)
 
 
+PATHS = ["fused", "three_kernels"]
+
+
+def _path_applies(path, dk):
+    """The fused recurrence + output kernel runs Dk in (64, 128]."""
+    if path == "fused" and dk <= 64:
+        pytest.skip("the fused kernel runs Dk in (64, 128]")
+
+
+@pytest.mark.parametrize("path", PATHS)
 @pytest.mark.parametrize("name", sorted(MANIFEST))
-def test_operator_on_reference_fixtures(name):
+def test_operator_on_reference_fixtures(name, path):
     dev = _cuda()
     m = MANIFEST[name]
     z = np.load(H.ROOT / "tests" / "golden" / f"gdr_{name}.npz")
+    _path_applies(path, z["q"].shape[-1])
     bf = lambda a: H.from_bits(a, dev)  # noqa: E731
     h0 = bf(z["h0"]) if z["h0"].dtype == np.uint16 else torch.from_numpy(z["h0"]).to(dev)
     g = torch.from_numpy(z["g"]).to(dev) if "g" in z.files else None
     asl = torch.from_numpy(z["seq_lens"]).to(dev)
     out, fin = cg.chunk_gated_delta_rule(bf(z["q"]), bf(z["k"]), bf(z["v"]), bf(z["beta"]), h0, asl, m["scale"], g,
-                                         check_device_status=True)
+                                         check_device_status=True, path=path)
     torch.cuda.synchronize()
     assert out.dtype == torch.bfloat16 and fin.dtype == h0.dtype
     check(out, fin, H.as_f32(z["golden_out"]), H.as_f32(z["golden_final"]), H.as_f32(z["bench_out"]),
@@ -80,13 +91,17 @@ def make_case(lens, nk, nv, dk, dv, state_dtype, seed, with_g=True):
     ([100, 37], 2, 4, 32, 32, torch.float32),
     ([150], 1, 2, 96, 48, torch.bfloat16),
     ([64, 65], 2, 2, 128, 80, torch.float32),
+    # several sequences of several chunks, partial last chunks
+    ([1000, 300, 64, 700], 2, 8, 128, 128, torch.float32),
 ])
-def test_operator_on_ragged_batches(lens, nk, nv, dk, dv, state):
+@pytest.mark.parametrize("path", PATHS)
+def test_operator_on_ragged_batches(lens, nk, nv, dk, dv, state, path):
     dev = _cuda()
+    _path_applies(path, dk)
     q, k, v, beta, g, h0, asl = make_case(lens, nk, nv, dk, dv, state, seed=sum(lens) + nv)
     scale = dk ** -0.5
     out, fin = cg.chunk_gated_delta_rule(q.to(dev), k.to(dev), v.to(dev), beta.to(dev), h0.to(dev), asl.to(dev), scale,
-                                         g.to(dev), check_device_status=True)
+                                         g.to(dev), check_device_status=True, path=path)
     torch.cuda.synchronize()
     f = H.as_f32
     bout, bfin, _ = G.benchmark_op(f(q), f(k), f(v), f(beta), scale, f(h0), lens, g.numpy())
@@ -94,12 +109,13 @@ def test_operator_on_ragged_batches(lens, nk, nv, dk, dv, state):
     check(out, fin, gout, gfin, bout, bfin)
 
 
-def test_operator_without_gate():
+@pytest.mark.parametrize("path", PATHS)
+def test_operator_without_gate(path):
     dev = _cuda()
     lens = [100, 37]
     q, k, v, beta, _, h0, asl = make_case(lens, 2, 2, 128, 128, torch.bfloat16, seed=5, with_g=False)
     out, fin = cg.chunk_gated_delta_rule(q.to(dev), k.to(dev), v.to(dev), beta.to(dev), h0.to(dev), asl.to(dev), None,
-                                         None, check_device_status=True)
+                                         None, check_device_status=True, path=path)
     torch.cuda.synchronize()
     f = H.as_f32
     bout, bfin, _ = G.benchmark_op(f(q), f(k), f(v), f(beta), 128 ** -0.5, f(h0), lens, None)
@@ -118,3 +134,25 @@ def test_lengths_not_summing_to_t_are_flagged():
     ws = torch.zeros(op.workspace_size, dtype=torch.uint8, device=dev)
     op(ws)
     assert cg.read_device_status(ws) & 0x2
+
+
+@pytest.mark.parametrize("lens,nk,nv,dv,state", [
+    ([4096, 4096], 8, 64, 128, torch.float32),           # the auto path's fused regime: B * Nv = 128
+    ([77, 0, 2000, 1, 640], 4, 8, 64, torch.bfloat16),   # V = 64, ragged, an empty sequence
+])
+def test_fused_matches_three_kernels(lens, nk, nv, dv, state):
+    """The two paths compute the same products; they differ only in how the
+    output's two fp32 terms are summed (one fma against an MMA accumulation),
+    so the bf16 outputs agree to the last bit nearly everywhere and the final
+    states (the same recurrence) exactly."""
+    dev = _cuda()
+    q, k, v, beta, g, h0, asl = make_case(lens, nk, nv, 128, dv, state, seed=11)
+    args = [x.to(dev) for x in (q, k, v, beta, h0, asl)]
+    o1, f1 = cg.chunk_gated_delta_rule(*args, None, g.to(dev), check_device_status=True, path="fused")
+    o2, f2 = cg.chunk_gated_delta_rule(*args, None, g.to(dev), check_device_status=True, path="three_kernels")
+    torch.cuda.synchronize()
+    assert torch.equal(f1, f2)
+    a, b = o1.float(), o2.float()
+    assert torch.isfinite(a).all()
+    assert (a == b).float().mean().item() >= 0.99
+    assert ((a - b).abs() <= 2 ** -7 * b.abs() + 1e-6).all()
