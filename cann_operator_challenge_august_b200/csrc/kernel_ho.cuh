@@ -409,31 +409,45 @@ __global__ void __launch_bounds__(HoConfig<VT>::kThreads, 1) fwd_ho_tc_kernel(co
             const float g_i = (p.g && orow < len) ? gs[orow] : 0.0f;
             const float f_o = __fmul_rn(sc, expf(g_i));
             {
+                // Lanes 16..31 hold the q rows of A; each 16-column block is split so that the
+                // lane pair (l, l^16), which shares row orow, computes 8 columns each: lanes
+                // 16..31 columns 0..7 of the block, lanes 0..15 columns 8..15 (one shuffle).
                 constexpr int kPCols = 64 / Cfg::EW;  // A columns per warp
                 const int pbase = kPCols * e;
+                const int half8 = lane < 16 ? 8 : 0;
 #pragma unroll
                 for (int blk = 0; blk < kPCols / 16; ++blk) {
                     uint32_t r[16];
                     tmem_ld_32x32b_x16(tmem + ((32u * q) << 16) + Cfg::kColA + static_cast<uint32_t>(pbase + 16 * blk), r);
                     tmem_wait_ld();
-                    if (lane >= 16) {
-                        uint32_t pk[8];
+                    uint32_t a[8];
 #pragma unroll
-                        for (int jj = 0; jj < 16; jj += 2) {
-                            const int j = pbase + 16 * blk + jj;
-                            const float gj0 = (p.g && j < len) ? gs[j] : 0.0f;
-                            const float gj1 = (p.g && j + 1 < len) ? gs[j + 1] : 0.0f;
-                            const float s0 = round_bf16(__uint_as_float(r[jj]));
-                            const float s1 = round_bf16(__uint_as_float(r[jj + 1]));
-                            const float x0 = (j <= orow) ? __fmul_rn(__fmul_rn(s0, sc), __expf(g_i - gj0)) : 0.0f;
-                            const float x1 = (j + 1 <= orow) ? __fmul_rn(__fmul_rn(s1, sc), __expf(g_i - gj1)) : 0.0f;
-                            pk[jj / 2] = pack_bf16x2(x0, x1);
-                        }
-                        uint8_t* prow = stage + Cfg::kOffWQ + orow * 128;
-                        const int c16 = (pbase + 16 * blk) >> 3;  // first 16-byte chunk of the block
-                        *reinterpret_cast<uint4*>(prow + (((c16 + 0) ^ (orow & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-                        *reinterpret_cast<uint4*>(prow + (((c16 + 1) ^ (orow & 7)) << 4)) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+                    for (int i = 0; i < 8; ++i) {
+                        const uint32_t other = __shfl_xor_sync(0xffffffffu, r[8 + i], 16);
+                        a[i] = lane < 16 ? other : r[i];
                     }
+                    const int j0 = pbase + 16 * blk + half8;  // first of this lane's 8 columns
+                    float gj[8];
+                    {
+                        const float4 g0 = *reinterpret_cast<const float4*>(gs + j0);
+                        const float4 g1 = *reinterpret_cast<const float4*>(gs + j0 + 4);
+                        gj[0] = g0.x; gj[1] = g0.y; gj[2] = g0.z; gj[3] = g0.w;
+                        gj[4] = g1.x; gj[5] = g1.y; gj[6] = g1.z; gj[7] = g1.w;
+                    }
+                    uint32_t pk[4];
+#pragma unroll
+                    for (int i = 0; i < 8; i += 2) {
+                        // bf16(A) for the pair in one conversion
+                        const float2 sb = unpack_bf16x2(pack_bf16x2(__uint_as_float(a[i]), __uint_as_float(a[i + 1])));
+                        const int j = j0 + i;
+                        const float e0 = __expf(g_i - ((p.g && j < len) ? gj[i] : 0.0f));
+                        const float e1 = __expf(g_i - ((p.g && j + 1 < len) ? gj[i + 1] : 0.0f));
+                        const float x0 = (j <= orow) ? __fmul_rn(__fmul_rn(sb.x, sc), e0) : 0.0f;
+                        const float x1 = (j + 1 <= orow) ? __fmul_rn(__fmul_rn(sb.y, sc), e1) : 0.0f;
+                        pk[i / 2] = pack_bf16x2(x0, x1);
+                    }
+                    uint8_t* prow = stage + Cfg::kOffWQ + orow * 128;
+                    *reinterpret_cast<uint4*>(prow + ((((j0 >> 3)) ^ (orow & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
                 }
             }
             fence_proxy_async_smem();
