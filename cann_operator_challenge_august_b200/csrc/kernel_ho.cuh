@@ -331,6 +331,15 @@ __global__ void __launch_bounds__(HoConfig<VT>::kThreads, 1) fwd_ho_tc_kernel(co
             }
         };
 
+        // swizzled byte offsets of this thread's (row, column pair) elements in the u / v_decay /
+        // v_new tiles (the same every chunk)
+        uint32_t offs[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const int cb = i >> 3, j = (i >> 1) & 3, half = i & 1;
+            offs[i] = sw128_off(half ? tb : ta, cbase + 32 * cb + 8 * j + pc, 8192);
+        }
+
         bool ok = true;
         write_state_tile();
         fence_proxy_async_smem();
@@ -362,12 +371,6 @@ __global__ void __launch_bounds__(HoConfig<VT>::kThreads, 1) fwd_ho_tc_kernel(co
                 alpha = expf(g_l);
             }
             uint8_t* ut = stage + Cfg::kOffU;
-            uint32_t offs[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                const int cb = i >> 3, j = (i >> 1) & 3, half = i & 1;
-                offs[i] = sw128_off(half ? tb : ta, cbase + 32 * cb + 8 * j + pc, 8192);
-            }
             uint32_t uraw[16];
 #pragma unroll
             for (int i = 0; i < 16; ++i) uraw[i] = *reinterpret_cast<const uint32_t*>(ut + offs[i]);
@@ -491,28 +494,23 @@ __global__ void __launch_bounds__(HoConfig<VT>::kThreads, 1) fwd_ho_tc_kernel(co
             tc_fence_after();
             uint32_t ov[32];  // this lane's row orow, columns cbase + 32*ohalf ..
             {
+                // lanes 0..15 hold O2 (rows 16q+lane), lanes 16..31 O1 (rows 16q+lane-16), all 64
+                // columns of the slice; lanes 0..15 store columns 0..31 and lanes 16..31 columns
+                // 32..63, so each lane sends its partner exactly the half the partner stores
+                uint32_t r[4][16];
+                const uint32_t base = tmem + ((32u * q) << 16) + d1col + static_cast<uint32_t>(cbase);
 #pragma unroll
-                for (int hh = 0; hh < 2; ++hh) {
-                    // lanes 0..15: O2 (rows 16q+lane), lanes 16..31: O1 (rows 16q+lane-16)
-                    uint32_t r[2][16];
-                    const uint32_t base = tmem + ((32u * q) << 16) + d1col + static_cast<uint32_t>(cbase + 32 * hh);
-                    tmem_ld_32x32b_x16(base, r[0]);
-                    tmem_ld_32x32b_x16(base + 16, r[1]);
-                    tmem_wait_ld();
+                for (int m = 0; m < 4; ++m) tmem_ld_32x32b_x16(base + 16 * m, r[m]);
+                tmem_wait_ld();
 #pragma unroll
-                    for (int j = 0; j < 2; ++j)
-#pragma unroll
-                        for (int i = 0; i < 16; ++i) {
-                            const float mine = __uint_as_float(r[j][i]);
-                            const float other = __shfl_xor_sync(0xffffffffu, mine, 16);
-                            if (hh == ohalf) {
-                                // half 0 is stored by lanes 0..15 (own O2, partner's O1), half 1 by
-                                // lanes 16..31 (own O1, partner's O2)
-                                const float o1 = ohalf ? mine : other;
-                                const float o2 = ohalf ? other : mine;
-                                ov[16 * j + i] = __float_as_uint(fmaf(f_o, o1, o2));
-                            }
-                        }
+                for (int i = 0; i < 32; ++i) {
+                    const uint32_t lo = r[i >> 4][i & 15], hi = r[2 + (i >> 4)][i & 15];
+                    // lane < 16 sends O2 columns 32+i, receives O1 columns i; lane >= 16 sends O1
+                    // columns i, receives O2 columns 32+i
+                    const float got = __uint_as_float(__shfl_xor_sync(0xffffffffu, ohalf ? lo : hi, 16));
+                    const float o1 = ohalf ? __uint_as_float(hi) : got;
+                    const float o2 = ohalf ? got : __uint_as_float(lo);
+                    ov[i] = __float_as_uint(fmaf(f_o, o1, o2));
                 }
             }
             tc_fence_before();
