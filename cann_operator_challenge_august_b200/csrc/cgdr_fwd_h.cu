@@ -277,15 +277,23 @@ cgdrStatus build(const cgdrTensor* k, const cgdrTensor* w, const cgdrTensor* u, 
     if (tc_ok) {
         int vt = opt.v_tile;
         if (vt == 0) {
-            // 64-column tiles while they fit one CTA per SM (the shortest chain);
-            // beyond that 128-column tiles, one CTA per SM: on B=4, T=8192, H=32,
-            // K=V=128 (256 64-column tasks) they take 0.288 ms against 0.307 ms
-            // for two 64-column CTAs per SM.
-            vt = (d.V % 128 == 0 && d.N * d.HV * (d.V / 64) > 148) ? 128 : 64;
+            // The narrowest tiles that still fit one CTA per SM: a (sequence, head) chain
+            // split over more SMs carries less epilogue work per chunk.  32-column tiles
+            // (K = 128) while they fit, then 64-column ones; beyond one CTA per SM
+            // 128-column tiles: on B=4, T=8192, H=32, K=V=128 (256 64-column tasks)
+            // they take 0.288 ms against 0.307 ms for two 64-column CTAs per SM.
+            if (d.K == 128 && d.V % 32 == 0 && d.N * d.HV * (d.V / 32) <= 148)
+                vt = 32;
+            else
+                vt = (d.V % 128 == 0 && d.N * d.HV * (d.V / 64) > 148) ? 128 : 64;
         }
-        if (vt != 64 && vt != 128) {
+        if (vt != 32 && vt != 64 && vt != 128) {
             delete ex_;
-            return fail(CGDR_STATUS_UNSUPPORTED, "v_tile must be 64 or 128 on the tensor-core path");
+            return fail(CGDR_STATUS_UNSUPPORTED, "v_tile must be 32, 64 or 128 on the tensor-core path");
+        }
+        if (vt == 32 && d.K != 128) {
+            delete ex_;
+            return fail(CGDR_STATUS_UNSUPPORTED, "v_tile 32 needs K = 128");
         }
         if (d.V % vt != 0) {
             delete ex_;
@@ -293,7 +301,7 @@ cgdrStatus build(const cgdrTensor* k, const cgdrTensor* w, const cgdrTensor* u, 
         }
         pl.kernel = 1;
         pl.v_tile = vt;
-        pl.stages = vt == 128 ? 3 : 2;
+        pl.stages = vt == 64 ? 2 : 3;
         pl.block = vt == 128 ? TcConfig<128, 128, 3, 2>::kThreads : TcConfig<128, 64, 2, 1>::kThreads;
     } else {
         if (d.K < 1 || d.K > kMaxHeadDim) {
@@ -314,7 +322,9 @@ cgdrStatus build(const cgdrTensor* k, const cgdrTensor* w, const cgdrTensor* u, 
     if (pl.kernel == 1) {
 #define CGDR_SMEM(K_, VT_, ST_, EW_) TcConfig<K_, VT_, ST_, EW_>::kSmemBytes
         if (d.K == 128)
-            pl.smem_bytes = pl.v_tile == 128 ? CGDR_SMEM(128, 128, 3, 2) : CGDR_SMEM(128, 64, 2, 1);
+            pl.smem_bytes = pl.v_tile == 128  ? CGDR_SMEM(128, 128, 3, 2)
+                            : pl.v_tile == 64 ? CGDR_SMEM(128, 64, 2, 1)
+                                              : CGDR_SMEM(128, 32, 3, 1);
         else
             pl.smem_bytes = pl.v_tile == 128 ? CGDR_SMEM(64, 128, 3, 2) : CGDR_SMEM(64, 64, 2, 1);
 #undef CGDR_SMEM
@@ -346,22 +356,26 @@ cgdrStatus build_maps(const cgdrExecutor* ex, TcMaps* m)
         const uint32_t box[4] = {64, 1, 64, 1};
         if ((st = make_map(&m->w, const_cast<void*>(p.w), 4, size, stride, box, "w"))) return st;
     }
+    // 32-column tiles move u, v_new and h in 32-column boxes with the 64-byte swizzle
+    const bool sw64 = ex->plan.v_tile == 32;
+    const uint32_t cols = sw64 ? 32 : 64;
+    const int swz = sw64 ? 64 : 128;
     {
         const int64_t size[4] = {p.V, p.H, p.T, p.B}, stride[4] = {1, p.u_sh, p.u_st, p.u_sb};
-        const uint32_t box[4] = {64, 1, 64, 1};
-        if ((st = make_map(&m->u, const_cast<void*>(p.u), 4, size, stride, box, "u"))) return st;
+        const uint32_t box[4] = {cols, 1, 64, 1};
+        if ((st = make_map(&m->u, const_cast<void*>(p.u), 4, size, stride, box, "u", swz))) return st;
     }
     if (p.v_new) {
         const int64_t size[4] = {p.V, p.H, p.T, p.B}, stride[4] = {1, p.v_sh, p.v_st, p.v_sb};
-        const uint32_t box[4] = {64, 1, 16, 1};
-        if ((st = make_map(&m->v, p.v_new, 4, size, stride, box, "v"))) return st;
+        const uint32_t box[4] = {cols, 1, 16, 1};
+        if ((st = make_map(&m->v, p.v_new, 4, size, stride, box, "v", swz))) return st;
     } else {
         memset(&m->v, 0, sizeof(m->v));
     }
     {
         const int64_t size[5] = {p.V, p.K, p.H, p.NT, p.B}, stride[5] = {1, p.h_sk, p.h_sh, p.h_sc, p.h_sb};
-        const uint32_t box[5] = {64, static_cast<uint32_t>(p.K == 128 ? 32 : 16), 1, 1, 1};
-        if ((st = make_map(&m->h, p.h, 5, size, stride, box, "h"))) return st;
+        const uint32_t box[5] = {cols, static_cast<uint32_t>(p.K == 128 ? 32 : 16), 1, 1, 1};
+        if ((st = make_map(&m->h, p.h, 5, size, stride, box, "h", swz))) return st;
     }
     return CGDR_STATUS_SUCCESS;
 }
@@ -493,8 +507,9 @@ cgdrStatus fwd_h_enqueue(const cgdrExecutor* executor, int* status, uint8_t* met
         args.p = p;
         const int grid = pl.grid;
         if (p.K == 128)
-            e = pl.v_tile == 128 ? launch_tc_numerics<128, 128, 3, 2>(args, grid, stream)
-                                 : launch_tc_numerics<128, 64, 2, 1>(args, grid, stream);
+            e = pl.v_tile == 128  ? launch_tc_numerics<128, 128, 3, 2>(args, grid, stream)
+                : pl.v_tile == 64 ? launch_tc_numerics<128, 64, 2, 1>(args, grid, stream)
+                                  : launch_tc_numerics<128, 32, 3, 1>(args, grid, stream);
         else
             e = pl.v_tile == 128 ? launch_tc_numerics<64, 128, 3, 2>(args, grid, stream)
                                  : launch_tc_numerics<64, 64, 2, 1>(args, grid, stream);

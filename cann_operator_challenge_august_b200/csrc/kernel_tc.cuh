@@ -45,20 +45,27 @@ struct TcArgs {
 template <int K_, int VT, int STAGES, int EW>
 struct TcConfig {
     static_assert(K_ == 64 || K_ == 128, "tensor-core path: K in {64, 128}");
-    static_assert(VT == 64 || VT == 128, "tensor-core path: V tile in {64, 128}");
+    static_assert(VT == 32 || VT == 64 || VT == 128, "tensor-core path: V tile in {32, 64, 128}");
     static_assert(EW == 1 || EW == VT / 64, "column split must be 1 or one warp per 64-column sub-tile");
+    static_assert(VT != 32 || K_ == 128, "32-column tiles: K = 128");
+    // 32-column tiles keep u_c, v_new and S in 64-byte rows (64-byte swizzle);
+    // wider tiles in 64-column sub-tiles of 128-byte rows (128-byte swizzle)
+    static constexpr bool kSw64 = VT == 32;
+    static constexpr int kRowB = kSw64 ? 64 : 128;      // bytes per row of a u_c / v_new / S sub-tile
+    static constexpr int kSubCols = kSw64 ? 32 : 64;     // columns per sub-tile
+    static constexpr int kUSub = 64 * kRowB;            // one sub-tile of u_c / v_new (64 token rows)
     static constexpr int kEpiWarps = 4 * EW;
     static constexpr int kThreads = 32 * (kEpiWarps + 2);
     static constexpr int kProducerWarp = kEpiWarps;
     static constexpr int kMmaWarp = kEpiWarps + 1;
     static constexpr int kCW = VT / EW;                 // columns per epilogue warp
     static constexpr int kSubK = K_ / 64;              // 64-column sub-tiles of k_c / w_c
-    static constexpr int kSubV = VT / 64;              // 64-column sub-tiles of u_c / S / v_new
+    static constexpr int kSubV = VT / kSubCols;         // sub-tiles of u_c / S / v_new
     static constexpr int kTileKBytes = K_ * 128;       // [64 tokens][K] bf16
     static constexpr int kTileUBytes = VT * 128;       // [64 tokens][VT] bf16
     static constexpr int kStageBytes = 2 * kTileKBytes + kTileUBytes;
     static constexpr int kSBytes = K_ * VT * 2;        // [K][VT] bf16
-    static constexpr int kSSubBytes = K_ * 128;        // one 64-column sub-tile of S
+    static constexpr int kSSubBytes = K_ * kRowB;      // one sub-tile of S
     static constexpr int kVoutBytes = 64 * VT * 2;
     static constexpr int kOffS = STAGES * kStageBytes;
     static constexpr int kOffVout = kOffS + kSBytes;
@@ -80,6 +87,28 @@ __device__ __forceinline__ uint32_t sw128_off(int row, int col, int sub_bytes)
 {
     const int sub = col >> 6, cc = col & 63;
     return sub * sub_bytes + row * 128 + ((((cc >> 3) ^ (row & 7)) & 7) << 4) + ((cc & 7) << 1);
+}
+
+// Byte offset of element (row, col) of a u_c / v_new / S tile: 128-byte swizzle in
+// 64-column sub-tiles, or (SW64) one 32-column tile of 64-byte rows whose
+// 16-byte chunks are XORed with (row / 2) % 4.
+template <bool SW64>
+__device__ __forceinline__ uint32_t tile_off(int row, int col, int sub_bytes)
+{
+    if constexpr (SW64)
+        return row * 64 + ((((col >> 3) ^ (row >> 1)) & 3) << 4) + ((col & 7) << 1);
+    else
+        return sw128_off(row, col, sub_bytes);
+}
+
+// MN-major operand descriptor of a u_c / v_new / S tile (see tile_off).
+template <bool SW64>
+__device__ __forceinline__ uint64_t umma_desc_mn(uint32_t saddr, uint32_t sub_bytes)
+{
+    if constexpr (SW64)
+        return umma_desc_sw64(saddr, sub_bytes, 512);
+    else
+        return umma_desc_sw128(saddr, sub_bytes, 1024);
 }
 
 __device__ __forceinline__ void cp_async_4(void* smem_dst, const void* gmem_src)
@@ -210,8 +239,8 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
                                 sub * 64, static_cast<int>(hv), t0, b);
 #pragma unroll
                 for (int sub = 0; sub < Cfg::kSubV; ++sub)
-                    tma_load_4d(&args.maps.u, smem + s * Cfg::kStageBytes + 2 * Cfg::kTileKBytes + sub * 8192,
-                                &full[s], v0 + sub * 64, static_cast<int>(hv), t0, b);
+                    tma_load_4d(&args.maps.u, smem + s * Cfg::kStageBytes + 2 * Cfg::kTileKBytes + sub * Cfg::kUSub,
+                                &full[s], v0 + sub * Cfg::kSubCols, static_cast<int>(hv), t0, b);
             }
             // gate inputs of the chunk: 64 fp32 values at any stride, 2 per lane
             if (p.g) {
@@ -248,23 +277,23 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
             tc_fence_after();
             // descriptors differ only in the start-address field (bits 0-13, 16-byte units)
             const uint64_t a1 = umma_desc_sw128(wc_addr(s), 16, 1024);
-            const uint64_t b1 = umma_desc_sw128(s_addr, Cfg::kSSubBytes, 1024);
+            const uint64_t b1 = umma_desc_mn<Cfg::kSw64>(s_addr, Cfg::kSSubBytes);
             if (elect_one_sync()) {
 #pragma unroll
                 for (int kk = 0; kk < K_ / 16; ++kk)
                     tc_mma_bf16(d1, a1 + static_cast<uint64_t>(((kk >> 2) * 8192 + (kk & 3) * 32) >> 4),
-                                b1 + static_cast<uint64_t>((kk * 2048) >> 4), Cfg::kIdesc1, kk > 0 ? 1u : 0u);
+                                b1 + static_cast<uint64_t>((kk * 16 * Cfg::kRowB) >> 4), Cfg::kIdesc1, kk > 0 ? 1u : 0u);
                 tc_commit(mma1_done);
             }
             __syncwarp();
             if (!wait_warp(vdec_ready, static_cast<uint32_t>(c) & 1)) break;
             tc_fence_after();
             const uint64_t a2 = umma_desc_sw128(kc_addr(s), 8192, 1024);
-            const uint64_t b2 = umma_desc_sw128(uc_addr(s), 8192, 1024);
+            const uint64_t b2 = umma_desc_mn<Cfg::kSw64>(uc_addr(s), Cfg::kUSub);
             if (elect_one_sync()) {
 #pragma unroll
                 for (int tt = 0; tt < 4; ++tt)
-                    tc_mma_bf16(d2, a2 + static_cast<uint64_t>((tt * 2048) >> 4), b2 + static_cast<uint64_t>((tt * 2048) >> 4),
+                    tc_mma_bf16(d2, a2 + static_cast<uint64_t>((tt * 2048) >> 4), b2 + static_cast<uint64_t>((tt * 16 * Cfg::kRowB) >> 4),
                                 Cfg::kIdesc2, tt > 0 ? 1u : 0u);
                 tc_commit(mma2_done);
                 tc_commit(&empty[s]);
@@ -368,7 +397,7 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
                     v.y = pack_bf16x2(st[8 * j + 2], st[8 * j + 3]);
                     v.z = pack_bf16x2(st[8 * j + 4], st[8 * j + 5]);
                     v.w = pack_bf16x2(st[8 * j + 6], st[8 * j + 7]);
-                    *reinterpret_cast<uint4*>(s_tile + sw128_off(row, cbase + 8 * j, Cfg::kSSubBytes)) = v;
+                    *reinterpret_cast<uint4*>(s_tile + tile_off<Cfg::kSw64>(row, cbase + 8 * j, Cfg::kSSubBytes)) = v;
                 }
             } else {
 #pragma unroll
@@ -385,8 +414,9 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
             if (lane == 0) {
 #pragma unroll
                 for (int sub = 0; sub < Cfg::kSubV; ++sub) {
-                    if (sub * 64 < cbase || sub * 64 >= cbase + Cfg::kCW) continue;
-                    tma_store_5d(&args.maps.h, s_tile + sub * Cfg::kSSubBytes + Cfg::kHRows * q * 128, v0 + sub * 64,
+                    if (sub * Cfg::kSubCols < cbase || sub * Cfg::kSubCols >= cbase + Cfg::kCW) continue;
+                    tma_store_5d(&args.maps.h, s_tile + sub * Cfg::kSSubBytes + Cfg::kHRows * q * Cfg::kRowB,
+                                 v0 + sub * Cfg::kSubCols,
                                  Cfg::kHRows * q, static_cast<int>(hv), static_cast<int>(si.boh + chunk),
                                  static_cast<int>(si.b));
                 }
@@ -397,7 +427,7 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
         constexpr int kPairs = (Cfg::kCW / 32) * 8;  // (column block, 8-column group, row half)
         // Pack v_new after MMA2 is released (64-column tiles); the 10-warp 128-column
         // configuration packs it with v_decay to stay within its register budget.
-        constexpr bool kDeferVnew = VT == 64;
+        constexpr bool kDeferVnew = VT <= 64;
 
         bool ok = true;
         write_state_tile();
@@ -444,7 +474,7 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
 #pragma unroll
             for (int i = 0; i < kPairs; ++i) {
                 const int cb = i >> 3, j = (i >> 1) & 3, half = i & 1;
-                offs[i] = sw128_off(half ? tb : ta, cbase + 32 * cb + 8 * j + pc, 8192);
+                offs[i] = tile_off<Cfg::kSw64>(half ? tb : ta, cbase + 32 * cb + 8 * j + pc, Cfg::kUSub);
             }
             uint32_t uraw[kPairs], vds[kPairs], vns[kPairs], vos[kPairs];
 #pragma unroll
@@ -563,8 +593,8 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
                 if (lane == 0) {
 #pragma unroll
                     for (int sub = 0; sub < Cfg::kSubV; ++sub) {
-                        if (sub * 64 < cbase || sub * 64 >= cbase + Cfg::kCW) continue;
-                        tma_store_4d(&args.maps.v, vout + sub * 8192 + 16 * q * 128, v0 + sub * 64,
+                        if (sub * Cfg::kSubCols < cbase || sub * Cfg::kSubCols >= cbase + Cfg::kCW) continue;
+                        tma_store_4d(&args.maps.v, vout + sub * Cfg::kUSub + 16 * q * Cfg::kRowB, v0 + sub * Cfg::kSubCols,
                                      static_cast<int>(hv), static_cast<int>(t0 + 16 * q), static_cast<int>(si.b));
                     }
                     bulk_commit_group();

@@ -259,6 +259,19 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr, uint32_t lbo
     return d;
 }
 
+// The same with the 64-byte swizzle (layout type 4): 64-byte rows, 8-row groups
+// `sbo` apart; for MN-major operands one atom is 32 elements wide.
+__device__ __forceinline__ uint64_t umma_desc_sw64(uint32_t saddr, uint32_t lbo, uint32_t sbo)
+{
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+    d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+    d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+    d |= 1ull << 46;  // descriptor version for tcgen05
+    d |= 4ull << 61;  // SWIZZLE_64B
+    return d;
+}
+
 // Instruction descriptor for kind::f16 with bf16 A/B and fp32 D.
 __host__ __device__ constexpr uint32_t umma_idesc_bf16(int M, int N, bool a_mn_major, bool b_mn_major)
 {

@@ -188,7 +188,7 @@ def test_plan_varlen_all_optional_paths():
     assert pl["plan_key"] == 7  # has_init | varlen<<1 | store_final<<2 (tiling.cpp:255-259)
     assert (pl["total_tokens"], pl["sequence_count"], pl["chunk_count"]) == (10016, 2, 158)
     assert (pl["value_heads"], pl["key_heads"], pl["head_ratio"]) == (8, 2, 4)
-    assert pl["kernel"] == 1 and pl["v_tile"] in (64, 128)
+    assert pl["kernel"] == 1 and pl["v_tile"] in (32, 64, 128)
     assert pl["task_count"] == 2 * 8 * pl["v_tile_count"] == pl["grid"]
     assert pl["workspace_bytes"] >= 256 + 4 * 3 + 4 * 2
 
@@ -252,3 +252,28 @@ def test_python_front_end_refuses_cpu_tensors():
     k = torch.zeros(1, 64, 1, 64, dtype=BF)
     with pytest.raises(ValueError, match="CUDA"):
         cg.chunk_gated_delta_rule_fwd_h(k, k, k, torch.zeros(1, 64, 1))
+
+
+@pytest.mark.parametrize("B,H,K,V,expected", [
+    (2, 16, 128, 128, 32),   # 32 pairs: 128 tasks of 32 columns fit one CTA per SM
+    (1, 32, 128, 128, 32),
+    (2, 32, 128, 128, 64),   # 64 pairs: 32-column tiles would need 256 CTAs
+    (4, 32, 128, 128, 128),  # 128 pairs: 64-column tiles would put two CTAs on an SM
+    (2, 16, 64, 64, 64),     # K = 64 runs 64- or 128-column tiles only
+])
+def test_plan_v_tile_choice(B, H, K, V, expected):
+    """The planner takes the narrowest V tile that keeps one CTA per SM (148 SMs)."""
+    T = 256
+    op = cg.ChunkGatedDeltaRuleFwdH(e((B, T, H, K)), e((B, T, H, K)), e((B, T, H, V)), e((B, T, H), F32), None,
+                                    None, None, 64, e((B, T // 64, H, K, V)), e((B, T, H, V)), e((B, H, K, V), F32),
+                                    layout="token_major", numerics="fp32_state")
+    assert op.plan["v_tile"] == expected
+
+
+def test_plan_rejects_v_tile_32_with_k_64():
+    B, T, H = 1, 128, 2
+    with pytest.raises(cg.CgdrError) as ei:
+        cg.ChunkGatedDeltaRuleFwdH(e((B, T, H, 64)), e((B, T, H, 64)), e((B, T, H, 64)), e((B, T, H), F32), None,
+                                   None, None, 64, e((B, 2, H, 64, 64)), e((B, T, H, 64)), None,
+                                   layout="token_major", numerics="fp32_state", v_tile=32)
+    assert ei.value.status_name == "UNSUPPORTED"
