@@ -116,7 +116,7 @@ typedef struct {
                                         32<=K==V<=256, N<=4 limits
                                         (infershape.cpp:196-275) */
     int32_t force_kernel;            /* 0 auto, 1 tensor-core path, 2 general path */
-    int32_t v_tile;                  /* 0 auto; else 32/64/128 */
+    int32_t v_tile;                  /* 0 auto; else 32 (K = 128 only), 64 or 128 */
     int32_t wait_timeout_ms;         /* 0 = default (2000 ms): bound on every
                                         device-side wait before the kernel
                                         gives up and flags DEVICE_ERROR */
