@@ -442,6 +442,11 @@ def main() -> int:
     del out, h_out, v_out, f_out
 
     def e2e_step():
+        if "cu_seqlens" not in host:
+            # the host-memory front end: batch rows pipelined, copies in and out overlapped
+            cg.chunk_gated_delta_rule_fwd_h_host(host["k"], host["w"], host["u"], host["g"], host["initial_state"],
+                                                 device=dev, out=tuple(host_out), **opts)
+            return
         d = {n: (x.to(dev, non_blocking=True) if x is not None else None) for n, x in host.items()}
         o = cg.chunk_gated_delta_rule_fwd_h(d["k"], d["w"], d["u"], d["g"], d["initial_state"],
                                             cu_seqlens=d.get("cu_seqlens"), chunk_indices=d.get("chunk_indices"),

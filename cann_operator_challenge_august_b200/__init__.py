@@ -27,6 +27,7 @@ from .gdr import (  # noqa: F401
     chunk_gated_delta_rule,
     chunk_wy_fwd,
 )
+from .host import chunk_gated_delta_rule_fwd_h_host  # noqa: F401
 from ._lib import CgdrError, CgdrValueError  # noqa: F401
 
 __all__ = [
@@ -34,6 +35,7 @@ __all__ = [
     "ChunkGatedDeltaRuleFwdH",
     "chunk_capacity",
     "chunk_gated_delta_rule_fwd_h",
+    "chunk_gated_delta_rule_fwd_h_host",
     "prepare_chunk_indices",
     "prepare_chunk_offsets",
     "read_device_status",
