@@ -18,7 +18,8 @@ inputs resident in HBM; inputs and outputs total ~1.9 GB per rank, far
 beyond the 126 MB L2, so no flush is needed between steps.  ``e2e`` is the
 same metric through the public Python API with pinned host buffers, the
 host->device copy of every input and the device->host copy of every output
-inside the timed region.  ``roofline`` relates the op's algorithmic HBM
+inside the timed region (fixed-length batches through the host-memory front
+end, which overlaps the two directions of copies with the kernels).  ``roofline`` relates the op's algorithmic HBM
 bytes per launch to the measured HBM copy bandwidth.  ``cpu_baseline`` is
 the reference's arithmetic (the CPU oracle, a restatement of the reference
 PyTorch code) timed on this host's cores on a bounded sample.
