@@ -18,8 +18,8 @@ inputs resident in HBM; inputs and outputs total ~1.9 GB per rank, far
 beyond the 126 MB L2, so no flush is needed between steps.  ``e2e`` is the
 same metric through the public Python API with pinned host buffers, the
 host->device copy of every input and the device->host copy of every output
-inside the timed region (fixed-length batches through the host-memory front
-end, which overlaps the two directions of copies with the kernels).  ``roofline`` relates the op's algorithmic HBM
+inside the timed region (through the host-memory front end, which overlaps
+the two directions of copies with the kernels).  ``roofline`` relates the op's algorithmic HBM
 bytes per launch to the measured HBM copy bandwidth.  ``cpu_baseline`` is
 the reference's arithmetic (the CPU oracle, a restatement of the reference
 PyTorch code) timed on this host's cores on a bounded sample.
@@ -436,24 +436,19 @@ def main() -> int:
 
     # ---- e2e: public API with pinned host buffers, copies inside the timed region
     host = {n: (x.cpu().pin_memory() if x is not None else None) for n, x in inp.items()}
-    h2d = sum(x.numel() * x.element_size() for x in host.values() if x is not None)
+    # bytes the front end copies to the device (cu_seqlens is read on the host; the chunk
+    # list is derived from it)
+    h2d = sum(x.numel() * x.element_size() for n, x in host.items()
+              if x is not None and n not in ("cu_seqlens", "chunk_indices"))
     h_out, v_out, f_out = out
     host_out = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in (h_out, v_out, f_out)]
     d2h = sum(t.numel() * t.element_size() for t in host_out)
     del out, h_out, v_out, f_out
 
     def e2e_step():
-        if "cu_seqlens" not in host:
-            # the host-memory front end: batch rows pipelined, copies in and out overlapped
-            cg.chunk_gated_delta_rule_fwd_h_host(host["k"], host["w"], host["u"], host["g"], host["initial_state"],
-                                                 device=dev, out=tuple(host_out), **opts)
-            return
-        d = {n: (x.to(dev, non_blocking=True) if x is not None else None) for n, x in host.items()}
-        o = cg.chunk_gated_delta_rule_fwd_h(d["k"], d["w"], d["u"], d["g"], d["initial_state"],
-                                            cu_seqlens=d.get("cu_seqlens"), chunk_indices=d.get("chunk_indices"),
-                                            **opts)
-        for dst, src in zip(host_out, o):
-            dst.copy_(src, non_blocking=True)
+        # the host-memory front end: pieces of the batch pipelined, copies in and out overlapped
+        cg.chunk_gated_delta_rule_fwd_h_host(host["k"], host["w"], host["u"], host["g"], host["initial_state"],
+                                             host.get("cu_seqlens"), device=dev, out=tuple(host_out), **opts)
 
     e2e_ms = e2e_value = None
     if args.e2e_steps > 0:

@@ -5,9 +5,10 @@ A caller whose tensors live in host memory would otherwise copy every input to
 the device, run the op and copy every output back, one after the other: on the
 north-star workload that is 0.82 GB in and 0.81 GB out around a 0.27 ms
 kernel, so the PCIe copies are the whole cost.  PCIe carries both directions at
-once, so this front end pipelines pieces of a fixed-length batch: each batch
-row (sequence), split along T at chunk boundaries into ranges of about 48 MB of
-input, a range continuing from the previous range's final state.  Piece i+1 is
+once, so this front end pipelines pieces of the batch: each sequence (a batch
+row, or a sequence of a packed varlen batch), split along T at chunk boundaries
+into ranges of about 48 MB of input, a range continuing from the previous
+range's final state.  Piece i+1 is
 copied in on one stream while piece i computes on a second stream and piece i-1
 is copied out on a third. Two device slots per tensor are
 recycled, and each stream waits on CUDA events. The caller's current stream
@@ -18,8 +19,7 @@ The kernels are the same as chunk_gated_delta_rule_fwd_h's, piece by piece (a
 row is an independent problem: its own sequence, initial and final state; a
 range of chunks starts from the state the kernel carries across the chunk
 boundary, fp32, or bf16-valued in the reference arithmetic, which fp32 holds
-exactly), so the outputs are bit-identical to the device API's.  Packed varlen batches are not
-split: copy them to the device and call chunk_gated_delta_rule_fwd_h.
+exactly), so the outputs are bit-identical to the device API's.
 """
 
 from __future__ import annotations
@@ -41,6 +41,25 @@ def _streams(device: torch.device):
     return _STREAMS[idx]
 
 
+def plan_pieces(seqs, tok_bytes: int, piece_bytes: int):
+    """Pipeline pieces of the problems ``seqs`` = [(batch row, first token, tokens,
+    first chunk in h, state row)]: each non-empty sequence split at chunk boundaries
+    into balanced ranges of about ``piece_bytes`` of input (``tok_bytes`` per token).
+    Returns [(batch row, first token, end token, first chunk in h, state row, first
+    range of its sequence, last range of its sequence)]."""
+    pieces = []
+    for (b, a, L, c, n) in seqs:
+        if L <= 0:
+            continue
+        nch = (L + CHUNK_SIZE - 1) // CHUNK_SIZE
+        parts = max(1, min(nch, round(L * tok_bytes / piece_bytes)))
+        per_s = (nch + parts - 1) // parts * CHUNK_SIZE  # tokens per range, balanced
+        ranges = [(t0, min(L, t0 + per_s)) for t0 in range(0, L, per_s)]
+        for j, (t0, t1) in enumerate(ranges):
+            pieces.append((b, a + t0, a + t1, c + t0 // CHUNK_SIZE, n, j == 0, j == len(ranges) - 1))
+    return pieces
+
+
 def _host_empty(shape, dtype, pin: bool):
     return torch.empty(shape, dtype=dtype, pin_memory=pin)
 
@@ -51,6 +70,7 @@ def chunk_gated_delta_rule_fwd_h_host(
     u: torch.Tensor,
     g: torch.Tensor | None = None,
     initial_state: torch.Tensor | None = None,
+    cu_seqlens: torch.Tensor | None = None,
     *,
     device: torch.device | str = "cuda",
     save_new_value: bool = True,
@@ -60,20 +80,22 @@ def chunk_gated_delta_rule_fwd_h_host(
     out: tuple[torch.Tensor, torch.Tensor | None, torch.Tensor | None] | None = None,
     **plan_options,
 ) -> tuple[torch.Tensor, torch.Tensor | None, torch.Tensor | None]:
-    """chunk_gated_delta_rule_fwd_h on host tensors (fixed-length batches).
+    """chunk_gated_delta_rule_fwd_h on host tensors.
 
     k ``[B,T,Hg,K]``, w ``[B,T,H,K]``, u ``[B,T,H,V]``, g ``[B,T,H]`` fp32 and
-    initial_state ``[B,H,K,V]`` are CPU tensors with contiguous rows; they must
+    initial_state ``[N,H,K,V]`` are CPU tensors with contiguous rows; they must
     be pinned for the copies to overlap (pageable memory still works, without
-    overlap).  Returns CPU tensors h ``[B,NT,H,K,V]``, v_new ``[B,T,H,V]``
-    (``None`` if ``save_new_value`` is False) and final_state ``[B,H,K,V]``
-    (``None`` if ``output_final_state`` is False), pinned, or written into
-    ``out``.  The caller's current stream on ``device`` waits for the whole
+    overlap).  With ``cu_seqlens`` (a CPU int64 tensor ``[N+1]``, B = 1) the
+    batch is packed varlen, as for chunk_gated_delta_rule_fwd_h.  Returns CPU
+    tensors h ``[B,NT,H,K,V]`` (NT summed over the sequences when varlen),
+    v_new ``[B,T,H,V]`` (``None`` if ``save_new_value`` is False) and
+    final_state ``[N,H,K,V]`` (``None`` if ``output_final_state`` is False),
+    pinned, or written into ``out``.  The caller's current stream on ``device`` waits for the whole
     pipeline; synchronize it before reading the outputs on the host.
     ``plan_options`` (``v_tile``, ``force_kernel``, ...) pass through to
     :class:`ChunkGatedDeltaRuleFwdH`.
     """
-    for t in (k, w, u, g, initial_state):
+    for t in (k, w, u, g, initial_state, cu_seqlens):
         if t is not None and t.is_cuda:
             raise ValueError("chunk_gated_delta_rule_fwd_h_host takes host (CPU) tensors")
     dev = torch.device(device)
@@ -83,28 +105,55 @@ def chunk_gated_delta_rule_fwd_h_host(
         dev = torch.device("cuda", torch.cuda.current_device())
     B, T, Hg, K = k.shape
     H, V = u.shape[-2], u.shape[-1]
-    NT = (T + CHUNK_SIZE - 1) // CHUNK_SIZE
+    # the problems: (batch row, first token, tokens, first chunk in h, state row)
+    if cu_seqlens is None:
+        NT = (T + CHUNK_SIZE - 1) // CHUNK_SIZE
+        seqs = [(b, 0, T, 0, b) for b in range(B)]
+    else:
+        if B != 1:
+            raise ValueError("a varlen batch (cu_seqlens) has B = 1")
+        cu = [int(x) for x in cu_seqlens.tolist()]
+        if len(cu) < 2 or cu[0] != 0 or cu[-1] != T or any(b < a for a, b in zip(cu, cu[1:])):
+            raise ValueError("cu_seqlens must rise from 0 to T")
+        seqs, c = [], 0
+        for n, (a, b) in enumerate(zip(cu, cu[1:])):
+            seqs.append((0, a, b - a, c, n))
+            c += (b - a + CHUNK_SIZE - 1) // CHUNK_SIZE
+        NT = c
+    N = len(seqs)
     pin = k.is_pinned()
     if out is None:
         h_out = _host_empty((B, NT, H, K, V), k.dtype, pin)
         v_out = _host_empty((B, T, H, V), u.dtype, pin) if save_new_value else None
-        f_out = _host_empty((B, H, K, V), final_state_dtype, pin) if output_final_state else None
+        f_out = _host_empty((N, H, K, V), final_state_dtype, pin) if output_final_state else None
     else:
         h_out, v_out, f_out = out
-    ins = [x for x in (k, w, u, g, initial_state) if x is not None]
-    outs = [x for x in (h_out, v_out, f_out) if x is not None]
-    for t in ins + outs:
+    for t in [x for x in (k, w, u, g, h_out, v_out) if x is not None]:
         if t.shape[0] != B or not t[0].is_contiguous():
-            raise ValueError("every tensor needs B rows of contiguous memory")
+            raise ValueError("k, w, u, g, h and v_new need B rows of contiguous memory")
+    for t in [x for x in (initial_state, f_out) if x is not None]:
+        if t.shape[0] != N or not t[0].is_contiguous():
+            raise ValueError("initial_state and final_state need one contiguous row per sequence")
+    # an empty sequence's final state is its initial state, as the kernel loads it (the
+    # reference arithmetic keeps the state in bf16)
+    for (_, _, L, _, n) in seqs:
+        if L == 0 and f_out is not None:
+            if initial_state is None:
+                f_out[n].zero_()
+            elif numerics == "reference":
+                f_out[n].copy_(initial_state[n].to(torch.bfloat16))
+            else:
+                f_out[n].copy_(initial_state[n])
 
     # pieces: the rows, each split along T at chunk boundaries into ranges of about
     # kPieceBytes of input; a range continues from the previous range's final state (the
     # fp32 state the kernel would carry across that chunk boundary)
-    row_bytes = sum(x[0].numel() * x.element_size() for x in (k, w, u) + ((g,) if g is not None else ()))
-    parts = max(1, min(NT, round(row_bytes / _PIECE_BYTES)))
-    per = (NT + parts - 1) // parts * CHUNK_SIZE  # tokens per range (a multiple of the chunk size)
-    ranges = [(t0, min(T, t0 + per)) for t0 in range(0, T, per)]
-    pieces = [(b, t0, t1, j == 0, j == len(ranges) - 1) for b in range(B) for j, (t0, t1) in enumerate(ranges)]
+    tok_bytes = sum(x[0, 0].numel() * x.element_size() for x in (k, w, u) + ((g,) if g is not None else ()))
+    pieces = plan_pieces(seqs, tok_bytes, _PIECE_BYTES)
+    if not pieces:
+        return h_out, v_out, f_out
+    per = max(t1 - t0 for (_, t0, t1, _, _, _, _) in pieces)
+    per = (per + CHUNK_SIZE - 1) // CHUNK_SIZE * CHUNK_SIZE
 
     caller = torch.cuda.current_stream(dev)
     s_in, s_comp, s_out = _streams(dev)
@@ -129,17 +178,17 @@ def chunk_gated_delta_rule_fwd_h_host(
         copied_in = [torch.cuda.Event() for _ in range(2)]
         computed = [torch.cuda.Event() for _ in range(2)]
         copied_out = [torch.cuda.Event() for _ in range(2)]
-        for i, (b, t0, t1, first, last) in enumerate(pieces):
+        for i, (b, t0, t1, c0, srow, first, last) in enumerate(pieces):
             s = i % 2
             n = t1 - t0
-            c0, c1 = t0 // CHUNK_SIZE, (t1 + CHUNK_SIZE - 1) // CHUNK_SIZE
+            c1 = c0 + (n + CHUNK_SIZE - 1) // CHUNK_SIZE
             with torch.cuda.stream(s_in):
                 if i >= 2:
                     s_in.wait_event(computed[s])  # piece i-2 has read this input slot
                 for dst, src in zip(slot_in[s], tin):
                     dst[:, :n].copy_(src[b:b + 1, t0:t1], non_blocking=True)
                 if first and initial_state is not None:
-                    h0_dev[s].copy_(initial_state[b:b + 1], non_blocking=True)
+                    h0_dev[s].copy_(initial_state[srow:srow + 1], non_blocking=True)
                 copied_in[s].record(s_in)
             with torch.cuda.stream(s_comp):
                 s_comp.wait_event(copied_in[s])
@@ -168,7 +217,7 @@ def chunk_gated_delta_rule_fwd_h_host(
                 if v_out is not None:
                     v_out[b:b + 1, t0:t1].copy_(slot_v[s][:, :n], non_blocking=True)
                 if last and f_out is not None:
-                    f_out[b:b + 1].copy_(slot_f[s], non_blocking=True)
+                    f_out[srow:srow + 1].copy_(slot_f[s], non_blocking=True)
                 copied_out[s].record(s_out)
         caller.wait_stream(s_out)
         caller.wait_stream(s_comp)

@@ -277,3 +277,36 @@ def test_plan_rejects_v_tile_32_with_k_64():
                                    None, None, 64, e((B, 2, H, 64, 64)), e((B, T, H, 64)), None,
                                    layout="token_major", numerics="fp32_state", v_tile=32)
     assert ei.value.status_name == "UNSUPPORTED"
+
+
+# ---- host-memory front end: the pipeline's pieces (pure host logic) -------------
+
+def test_host_pieces_cover_every_chunk_once():
+    from cann_operator_challenge_august_b200.host import plan_pieces
+    # a packed varlen batch: empty, one-token, ragged and long sequences
+    lens = [0, 1, 300, 0, 4096, 63, 65]
+    seqs, a, c = [], 0, 0
+    for n, L in enumerate(lens):
+        seqs.append((0, a, L, c, n))
+        a += L
+        c += (L + 63) // 64
+    for piece_bytes in (1 << 10, 1 << 16, 1 << 30):
+        pieces = plan_pieces(seqs, tok_bytes=1000, piece_bytes=piece_bytes)
+        tokens = sorted((t0, t1) for (_, t0, t1, *_rest) in pieces)
+        covered = [t for (t0, t1) in tokens for t in range(t0, t1)]
+        assert covered == list(range(sum(lens)))  # every token once, in order
+        for (b, t0, t1, c0, n, first, last) in pieces:
+            s0 = seqs[n][1]
+            assert (t0 - s0) % 64 == 0 and c0 == seqs[n][3] + (t0 - s0) // 64  # chunk-aligned starts
+        for n, L in enumerate(lens):
+            mine = [p for p in pieces if p[4] == n]
+            assert len(mine) == (0 if L == 0 else len(mine))
+            if L:
+                assert mine[0][5] and mine[-1][6] and sum(p[5] for p in mine) == 1 and sum(p[6] for p in mine) == 1
+
+
+def test_host_pieces_are_balanced():
+    from cann_operator_challenge_august_b200.host import plan_pieces
+    # one 8192-token row at ~24.7 KB per token: four ranges of 2048 tokens
+    pieces = plan_pieces([(0, 0, 8192, 0, 0)], tok_bytes=24704, piece_bytes=48 << 20)
+    assert [(t0, t1) for (_, t0, t1, *_r) in pieces] == [(0, 2048), (2048, 4096), (4096, 6144), (6144, 8192)]

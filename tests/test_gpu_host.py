@@ -22,12 +22,12 @@ def _cuda():
 
 
 @pytest.mark.parametrize("numerics", ["fp32_state", "reference"])
-@pytest.mark.parametrize("piece_bytes", [None, 1 << 20])
+@pytest.mark.parametrize("piece_bytes", [None, 1 << 16])
 @pytest.mark.parametrize("pinned", [True, False])
 @pytest.mark.parametrize("B,T,H,K,V", [(3, 333, 4, 128, 128), (5, 128, 2, 64, 64), (1, 1000, 2, 128, 64)])
 def test_host_api_matches_device_api(pinned, B, T, H, K, V, piece_bytes, numerics, monkeypatch):
-    """Whole rows, and rows split into ranges of chunks (1 MB pieces) that continue from
-    the previous range's final state."""
+    """Whole rows, and rows split into ranges of chunks (64 KB pieces: several per row)
+    that continue from the previous range's final state."""
     dev = _cuda()
     if piece_bytes is not None:
         monkeypatch.setattr(host_mod, "_PIECE_BYTES", piece_bytes)
@@ -73,3 +73,26 @@ def test_host_api_rejects_device_tensors():
     inp = helpers.make_inputs(1, 64, 1, 64, 64, seed=3, device=dev)
     with pytest.raises(ValueError):
         cg.chunk_gated_delta_rule_fwd_h_host(inp["k"], inp["w"], inp["u"], inp["g"], inp["initial_state"])
+
+
+@pytest.mark.parametrize("piece_bytes", [None, 1 << 16])
+@pytest.mark.parametrize("numerics", ["fp32_state", "reference"])
+def test_host_api_varlen(piece_bytes, numerics, monkeypatch):
+    """Packed varlen batch with an empty sequence, a one-token sequence and long
+    sequences split into several pieces."""
+    dev = _cuda()
+    if piece_bytes is not None:
+        monkeypatch.setattr(host_mod, "_PIECE_BYTES", piece_bytes)
+    cu = [0, 300, 300, 301, 1000, 1130]
+    inp = helpers.make_inputs(1, 1130, 4, 128, 128, seed=9, cu_seqlens=cu)
+    host = {n: x.pin_memory() for n, x in inp.items() if x is not None}
+    h, v, f = cg.chunk_gated_delta_rule_fwd_h_host(host["k"], host["w"], host["u"], host["g"], host["initial_state"],
+                                                   host["cu_seqlens"], device=dev, numerics=numerics)
+    torch.cuda.synchronize()
+    d = {n: x.to(dev) for n, x in host.items()}
+    h2, v2, f2 = cg.chunk_gated_delta_rule_fwd_h(d["k"], d["w"], d["u"], d["g"], d["initial_state"],
+                                                 cu_seqlens=d["cu_seqlens"], check_device_status=True,
+                                                 numerics=numerics)
+    torch.cuda.synchronize()
+    assert h.shape == h2.shape
+    assert torch.equal(h, h2.cpu()) and torch.equal(v, v2.cpu()) and torch.equal(f, f2.cpu())
