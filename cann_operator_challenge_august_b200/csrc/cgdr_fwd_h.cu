@@ -265,7 +265,8 @@ cgdrStatus build(const cgdrTensor* k, const cgdrTensor* w, const cgdrTensor* u, 
             if ((t->strides[i] * 2) % 16 != 0) return false;
         return true;
     };
-    bool tc_ok = io == kBF16 && (d.K == 64 || d.K == 128) && d.V % 64 == 0 && al16(k->data) && al16(w->data) &&
+    bool tc_ok = io == kBF16 && (d.K == 64 || d.K == 128) && (d.V % 64 == 0 || (d.K == 128 && d.V % 32 == 0)) &&
+                 al16(k->data) && al16(w->data) &&
                  al16(u->data) && al16(h->data) && st16(k) && st16(w) && st16(u) && st16(h) &&
                  (!present(v) || (al16(v->data) && st16(v))) && d.T < (int64_t(1) << 31) &&
                  d.NT < (int64_t(1) << 31);
@@ -282,7 +283,7 @@ cgdrStatus build(const cgdrTensor* k, const cgdrTensor* w, const cgdrTensor* u, 
             // (K = 128) while they fit, then 64-column ones; beyond one CTA per SM
             // 128-column tiles: on B=4, T=8192, H=32, K=V=128 (256 64-column tasks)
             // they take 0.288 ms against 0.307 ms for two 64-column CTAs per SM.
-            if (d.K == 128 && d.V % 32 == 0 && d.N * d.HV * (d.V / 32) <= 148)
+            if (d.K == 128 && d.V % 32 == 0 && (d.V % 64 != 0 || d.N * d.HV * (d.V / 32) <= 148))
                 vt = 32;
             else
                 vt = (d.V % 128 == 0 && d.N * d.HV * (d.V / 64) > 148) ? 128 : 64;

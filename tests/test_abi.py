@@ -260,6 +260,7 @@ def test_python_front_end_refuses_cpu_tensors():
     (2, 32, 128, 128, 64),   # 64 pairs: 32-column tiles would need 256 CTAs
     (4, 32, 128, 128, 128),  # 128 pairs: 64-column tiles would put two CTAs on an SM
     (2, 16, 64, 64, 64),     # K = 64 runs 64- or 128-column tiles only
+    (4, 32, 128, 96, 32),    # V % 64 != 0 (K = 128): 32-column tiles whatever the task count
 ])
 def test_plan_v_tile_choice(B, H, K, V, expected):
     """The planner takes the narrowest V tile that keeps one CTA per SM (148 SMs)."""

@@ -407,3 +407,19 @@ def test_v_tiles_agree(numerics, varlen, V, HK):
     for vt, o in zip((64, 128), outs[1:]):
         for name, a, b in zip(("h", "v", "final"), outs[0], o):
             assert torch.equal(a, b), f"v_tile 32 vs {vt}: {name} differs"
+
+
+@pytest.mark.parametrize("V", [32, 96])
+def test_value_width_multiple_of_32(V):
+    """K = 128 with V % 64 != 0 runs on the tensor cores in 32-column tiles: within the
+    north-star tolerance of the reference semantics, and near the general kernel."""
+    dev = _cuda()
+    inp = H.make_inputs(2, 300, 4, 128, V, seed=31)
+    h, v, f = _run_fla(inp, dev, force_kernel=1)
+    rh, rv, rf = H.oracle_run(inp, "reference", final_dtype="f32")
+    H.assert_close(h, rh, BF_TOL, BF_TOL, f"V{V}/h")
+    H.assert_close(v, rv, BF_TOL, BF_TOL, f"V{V}/v")
+    H.assert_close(f, rf, BF_TOL, BF_TOL, f"V{V}/final")
+    oh, ov, of = H.oracle_run(inp, "fp32_state")
+    H.assert_close(h, oh, BF_TOL, BF_TOL, f"V{V}/h fp32")
+    H.assert_close(f, of, BF_TOL, BF_TOL, f"V{V}/final fp32")
