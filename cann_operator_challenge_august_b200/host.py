@@ -103,7 +103,7 @@ def chunk_gated_delta_rule_fwd_h_host(
         raise ValueError("device must be a CUDA device")
     if dev.index is None:
         dev = torch.device("cuda", torch.cuda.current_device())
-    B, T, Hg, K = k.shape
+    B, T, _, K = k.shape
     H, V = u.shape[-2], u.shape[-1]
     # the problems: (batch row, first token, tokens, first chunk in h, state row)
     if cu_seqlens is None:
