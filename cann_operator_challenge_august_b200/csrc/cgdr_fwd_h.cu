@@ -53,6 +53,13 @@ struct Dims {
 
 int io_of(int32_t dt) { return dt == CGDR_DT_BF16 ? kBF16 : (dt == CGDR_DT_FLOAT32 ? kF32 : 0); }
 
+// K tile of the tensor-core kernel for head width K (0: no tensor-core kernel).
+int tc_k_tile(int64_t K)
+{
+    if (K < 8 || K > 256 || K % 8 != 0) return 0;
+    return K <= 64 ? 64 : K <= 128 ? 128 : 256;
+}
+
 cgdrStatus build(const cgdrTensor* k, const cgdrTensor* w, const cgdrTensor* u, const cgdrTensor* g,
                  const cgdrTensor* h0, const cgdrTensor* cu, const cgdrTensor* ci, const cgdrTensor* co,
                  int64_t chunk_size, const cgdrTensor* h, const cgdrTensor* v, const cgdrTensor* fin,
@@ -257,16 +264,19 @@ cgdrStatus build(const cgdrTensor* k, const cgdrTensor* w, const cgdrTensor* u, 
     pl.numerics = opt.numerics;
     pl.layout = opt.layout;
 
-    // Tensor-core path eligibility: bf16 I/O, K in {64, 128}, V a multiple of
-    // 64, TMA-describable strides (16-byte multiples) and aligned bases.
+    // Tensor-core path eligibility: bf16 I/O, K and V multiples of 8 with K <= 256,
+    // TMA-describable strides (16-byte multiples) and aligned bases.  The kernel's K
+    // tile is the next of 64, 128 and 256: k_c and w_c columns past K arrive
+    // zero-filled from the tensor maps, so the padded rows of the state stay zero and
+    // are never stored; a V tile that runs past V is clipped the same way.
     auto al16 = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };
     auto st16 = [](const cgdrTensor* t) {
         for (int i = 0; i < t->ndim - 1; ++i)
             if ((t->strides[i] * 2) % 16 != 0) return false;
         return true;
     };
-    bool tc_ok = io == kBF16 && (d.K == 64 || d.K == 128) && (d.V % 64 == 0 || (d.K == 128 && d.V % 32 == 0)) &&
-                 al16(k->data) && al16(w->data) &&
+    const int kt = tc_k_tile(d.K);
+    bool tc_ok = io == kBF16 && kt > 0 && d.V % 8 == 0 && al16(k->data) && al16(w->data) &&
                  al16(u->data) && al16(h->data) && st16(k) && st16(w) && st16(u) && st16(h) &&
                  (!present(v) || (al16(v->data) && st16(v))) && d.T < (int64_t(1) << 31) &&
                  d.NT < (int64_t(1) << 31);
@@ -276,34 +286,39 @@ cgdrStatus build(const cgdrTensor* k, const cgdrTensor* w, const cgdrTensor* u, 
         return fail(CGDR_STATUS_UNSUPPORTED, "tensor-core path requested but not applicable to these shapes/strides");
     }
     if (tc_ok) {
+        auto tasks = [&](int vt) { return d.N * d.HV * ((d.V + vt - 1) / vt); };
         int vt = opt.v_tile;
         if (vt == 0) {
             // The narrowest tiles that still fit one CTA per SM: a (sequence, head) chain
             // split over more SMs carries less epilogue work per chunk.  32-column tiles
-            // (K = 128) while they fit, then 64-column ones; beyond one CTA per SM
+            // (K tile 128) while they fit, then 64-column ones; beyond one CTA per SM
             // 128-column tiles: on B=4, T=8192, H=32, K=V=128 (256 64-column tasks)
-            // they take 0.288 ms against 0.307 ms for two 64-column CTAs per SM.
-            if (d.K == 128 && d.V % 32 == 0 && (d.V % 64 != 0 || d.N * d.HV * (d.V / 32) <= 148))
+            // they take 0.288 ms against 0.307 ms for two 64-column CTAs per SM.  The
+            // K tile 256 runs 64-column tiles only (its shared memory holds no wider).
+            if (kt == 256)
+                vt = 64;
+            else if (kt == 128 && (d.V % 64 != 0 || tasks(32) <= 148))
                 vt = 32;
             else
-                vt = (d.V % 128 == 0 && d.N * d.HV * (d.V / 64) > 148) ? 128 : 64;
+                vt = (d.V % 128 == 0 && tasks(64) > 148) ? 128 : 64;
         }
         if (vt != 32 && vt != 64 && vt != 128) {
             delete ex_;
             return fail(CGDR_STATUS_UNSUPPORTED, "v_tile must be 32, 64 or 128 on the tensor-core path");
         }
-        if (vt == 32 && d.K != 128) {
+        if (vt == 32 && kt != 128) {
             delete ex_;
-            return fail(CGDR_STATUS_UNSUPPORTED, "v_tile 32 needs K = 128");
+            return fail(CGDR_STATUS_UNSUPPORTED, "v_tile 32 needs 64 < K <= 128");
         }
-        if (d.V % vt != 0) {
+        if (kt == 256 && vt != 64) {
             delete ex_;
-            return fail(CGDR_STATUS_UNSUPPORTED, "V=%lld is not a multiple of v_tile=%d", static_cast<long long>(d.V), vt);
+            return fail(CGDR_STATUS_UNSUPPORTED, "K > 128 runs 64-column V tiles only");
         }
         pl.kernel = 1;
         pl.v_tile = vt;
-        pl.stages = vt == 64 ? 2 : 3;
-        pl.block = vt == 128 ? TcConfig<128, 128, 3, 2>::kThreads : TcConfig<128, 64, 2, 1>::kThreads;
+        pl.stages = (vt == 64) ? 2 : 3;
+        pl.block = kt == 256 ? TcConfig<256, 64, 2, 2>::kThreads
+                   : vt == 128 ? TcConfig<128, 128, 3, 2>::kThreads : TcConfig<128, 64, 2, 1>::kThreads;
     } else {
         if (d.K < 1 || d.K > kMaxHeadDim) {
             delete ex_;
@@ -322,7 +337,9 @@ cgdrStatus build(const cgdrTensor* k, const cgdrTensor* w, const cgdrTensor* u, 
     p.n_vtiles = static_cast<int32_t>(pl.v_tile_count);
     if (pl.kernel == 1) {
 #define CGDR_SMEM(K_, VT_, ST_, EW_) TcConfig<K_, VT_, ST_, EW_>::kSmemBytes
-        if (d.K == 128)
+        if (kt == 256)
+            pl.smem_bytes = CGDR_SMEM(256, 64, 2, 2);
+        else if (kt == 128)
             pl.smem_bytes = pl.v_tile == 128  ? CGDR_SMEM(128, 128, 3, 2)
                             : pl.v_tile == 64 ? CGDR_SMEM(128, 64, 2, 1)
                                               : CGDR_SMEM(128, 32, 3, 1);
@@ -367,15 +384,17 @@ cgdrStatus build_maps(const cgdrExecutor* ex, TcMaps* m)
         if ((st = make_map(&m->u, const_cast<void*>(p.u), 4, size, stride, box, "u", swz))) return st;
     }
     if (p.v_new) {
+        // the K tile 256 kernel stages v_new per warp in 32-column regions (64-byte swizzle)
+        const bool v32 = sw64 || tc_k_tile(p.K) == 256;
         const int64_t size[4] = {p.V, p.H, p.T, p.B}, stride[4] = {1, p.v_sh, p.v_st, p.v_sb};
-        const uint32_t box[4] = {cols, 1, 16, 1};
-        if ((st = make_map(&m->v, p.v_new, 4, size, stride, box, "v", swz))) return st;
+        const uint32_t box[4] = {v32 ? 32u : 64u, 1, 16, 1};
+        if ((st = make_map(&m->v, p.v_new, 4, size, stride, box, "v", v32 ? 64 : 128))) return st;
     } else {
         memset(&m->v, 0, sizeof(m->v));
     }
     {
         const int64_t size[5] = {p.V, p.K, p.H, p.NT, p.B}, stride[5] = {1, p.h_sk, p.h_sh, p.h_sc, p.h_sb};
-        const uint32_t box[5] = {cols, static_cast<uint32_t>(p.K == 128 ? 32 : 16), 1, 1, 1};
+        const uint32_t box[5] = {cols, static_cast<uint32_t>(tc_k_tile(p.K) == 64 ? 16 : 32), 1, 1, 1};
         if ((st = make_map(&m->h, p.h, 5, size, stride, box, "h", swz))) return st;
     }
     return CGDR_STATUS_SUCCESS;
@@ -507,7 +526,10 @@ cgdrStatus fwd_h_enqueue(const cgdrExecutor* executor, int* status, uint8_t* met
         if (st) return st;
         args.p = p;
         const int grid = pl.grid;
-        if (p.K == 128)
+        const int kt = tc_k_tile(p.K);
+        if (kt == 256)
+            e = launch_tc_numerics<256, 64, 2, 2>(args, grid, stream);
+        else if (kt == 128)
             e = pl.v_tile == 128  ? launch_tc_numerics<128, 128, 3, 2>(args, grid, stream)
                 : pl.v_tile == 64 ? launch_tc_numerics<128, 64, 2, 1>(args, grid, stream)
                                   : launch_tc_numerics<128, 32, 3, 1>(args, grid, stream);
@@ -670,9 +692,14 @@ extern "C" cgdrStatus cgdrChunkGatedDeltaRuleFwdHNoAlloc(cgdrExecutor* executor,
     }
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    if (e != cudaSuccess) {
         cgdrDestroyExecutor(executor);
         return fail(CGDR_STATUS_CUDA_ERROR, "cudaGetDevice: %s", cudaGetErrorString(e));
+    }
+    if (dev < 0 || dev >= kMaxDevices) {
+        cgdrDestroyExecutor(executor);
+        return fail(CGDR_STATUS_UNSUPPORTED, "device ordinal %d exceeds the %d devices this entry point serves", dev,
+                    kMaxDevices);
     }
     void* scratch = nullptr;
     {

@@ -44,10 +44,12 @@ struct TcArgs {
 
 template <int K_, int VT, int STAGES, int EW>
 struct TcConfig {
-    static_assert(K_ == 64 || K_ == 128, "tensor-core path: K in {64, 128}");
+    static_assert(K_ == 64 || K_ == 128 || K_ == 256, "tensor-core path: K tile in {64, 128, 256}");
     static_assert(VT == 32 || VT == 64 || VT == 128, "tensor-core path: V tile in {32, 64, 128}");
-    static_assert(EW == 1 || EW == VT / 64, "column split must be 1 or one warp per 64-column sub-tile");
+    static_assert(EW == 1 || EW == VT / 64 || (K_ == 256 && VT == 64 && EW == 2),
+                  "column split must be 1, one warp per 64-column sub-tile, or (K = 256) two 32-column halves");
     static_assert(VT != 32 || K_ == 128, "32-column tiles: K = 128");
+    static_assert(K_ != 256 || VT == 64, "K = 256: 64-column tiles");
     // 32-column tiles keep u_c, v_new and S in 64-byte rows (64-byte swizzle);
     // wider tiles in 64-column sub-tiles of 128-byte rows (128-byte swizzle)
     static constexpr bool kSw64 = VT == 32;
@@ -74,11 +76,26 @@ struct TcConfig {
     static constexpr int kNumBars = 2 * STAGES + 5;
     static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;  // + tmem slot, abort flag, alignment
     static constexpr uint32_t kStageTx = kStageBytes;
-    static constexpr int kTmemCols = 2 * VT;            // D1 at [0, VT), D2 at [VT, 2VT)
-    static constexpr int kHRows = (K_ == 128) ? 32 : 16;  // S rows per warp quadrant
-    static constexpr int kMinBlocks = (VT == 64) ? 2 : 1;  // CTAs resident per SM the tile is sized for
+    // MMA2 (M = K) as M = 128 halves when K = 256: D2 rows [128 m, 128 m + 128) at TMEM
+    // columns [VT (1 + m), VT (2 + m)).  D1 at [0, VT).
+    static constexpr int kM2 = K_ == 256 ? 128 : K_;
+    static constexpr int kM2Halves = K_ / kM2;
+    static constexpr int kTmemUsed = VT * (1 + kM2Halves);
+    static constexpr int kTmemCols = kTmemUsed <= 32 ? 32 : kTmemUsed <= 64 ? 64 : kTmemUsed <= 128 ? 128
+                                     : kTmemUsed <= 256 ? 256 : 512;
+    static constexpr int kHRows = (K_ == 64) ? 16 : 32;  // S rows per warp quadrant (h store box)
+    // Epilogue 2 (K >= 128): each thread owns one state row and kE2Cols of its columns.
+    // K = 256: warp w holds rows 128 (w / 4) + 32 (w % 4) + lane, all VT columns;
+    // K = 128: rows 32 (w % 4) + lane, the warp's epilogue-1 column slice.
+    static constexpr int kE2Cols = K_ == 256 ? VT : kCW;
+    // Epilogue-1 column slices narrower than a 64-column sub-tile (K = 256): each warp
+    // stages its v_new rows in a region of its own, 32 columns of 64-byte rows with the
+    // 64-byte swizzle, and stores it with a 32-column box, so no two warps share a store.
+    static constexpr bool kSplitVout = kCW < kSubCols;
+    static constexpr int kVoutRegion = 64 * 64;  // bytes of one warp's region (64 rows x 64 B)
+    static constexpr int kMinBlocks = (VT == 64 && K_ != 256) ? 2 : 1;  // CTAs resident per SM the tile is sized for
     static constexpr uint32_t kIdesc1 = umma_idesc_bf16(64, VT, false, true);
-    static constexpr uint32_t kIdesc2 = umma_idesc_bf16(K_, VT, true, true);
+    static constexpr uint32_t kIdesc2 = umma_idesc_bf16(kM2, VT, true, true);
 };
 
 // Byte offset of element (row, col) inside a swizzled tile made of 64-column
@@ -291,10 +308,14 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
             const uint64_t a2 = umma_desc_sw128(kc_addr(s), 8192, 1024);
             const uint64_t b2 = umma_desc_mn<Cfg::kSw64>(uc_addr(s), Cfg::kUSub);
             if (elect_one_sync()) {
+                // M = K halves (K = 256): rows 128 m.. of k_c start 2 m sub-tiles in
 #pragma unroll
-                for (int tt = 0; tt < 4; ++tt)
-                    tc_mma_bf16(d2, a2 + static_cast<uint64_t>((tt * 2048) >> 4), b2 + static_cast<uint64_t>((tt * 16 * Cfg::kRowB) >> 4),
-                                Cfg::kIdesc2, tt > 0 ? 1u : 0u);
+                for (int m = 0; m < Cfg::kM2Halves; ++m)
+#pragma unroll
+                    for (int tt = 0; tt < 4; ++tt)
+                        tc_mma_bf16(d2 + m * VT, a2 + static_cast<uint64_t>((m * 2 * 8192 + tt * 2048) >> 4),
+                                    b2 + static_cast<uint64_t>((tt * 16 * Cfg::kRowB) >> 4), Cfg::kIdesc2,
+                                    tt > 0 ? 1u : 0u);
                 tc_commit(mma2_done);
                 tc_commit(&empty[s]);
             }
@@ -319,14 +340,22 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
         const int pc = 2 * (lane & 3);        // column pair offset inside an 8-column group
 
         // State rows owned by this thread (epi2 fragment):
+        //   K=256: row 128e+32q+lane, columns [0, VT)
         //   K=128: row 32q+lane, columns cbase + [0, CW)
         //   K=64 : rows 16q+lane/4 (+8), columns cbase + 8j + pc + {0,1}
-        constexpr int kNState = (K_ == 128) ? Cfg::kCW : Cfg::kCW / 2;
+        // Rows at or beyond the caller's K (K < the tile's K_: k_c and w_c arrive
+        // zero-filled past K) stay zero and are never stored; so are columns at or
+        // beyond V in a partial V tile.
+        constexpr int kNState = (K_ >= 128) ? Cfg::kE2Cols : Cfg::kCW / 2;
+        const int e2_row = (K_ == 256 ? 128 * e : 0) + 32 * q + lane;  // K >= 128
+        const int e2_c0 = (K_ == 256) ? 0 : cbase;
+        const int kdim = static_cast<int>(p.K);
+        const int64_t vdim = p.V;
         float st[kNState];
         auto st_row_col = [&](int i, int& row, int& col) {
-            if constexpr (K_ == 128) {
-                row = 32 * q + lane;
-                col = cbase + i;
+            if constexpr (K_ >= 128) {
+                row = e2_row;
+                col = e2_c0 + i;
             } else {
                 // i = 4*j8 + 2*half + bit: j8 = 8-column group, half selects row +8
                 const int j8 = i >> 2, half = (i >> 1) & 1, bit = i & 1;
@@ -343,12 +372,14 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
         // kernel only: in the 64-column and reference-arithmetic kernels the extra
         // code slowed the chunk loop more than it saved (1.42 -> 1.52 ms on a
         // 1024-chunk chain; 0.52 -> 0.55 ms with the rounding chain).
-        constexpr bool kVecState = K_ == 128 && VT == 128 && !REF;
+        constexpr bool kVecState = ((K_ == 128 && VT == 128) || K_ == 256) && !REF;
         const size_t h0_esz = p.h0_dtype == kBF16 ? 2 : 4;
         const uint8_t* h0_run = nullptr;
+        // a whole run inside the caller's K x V state
+        const bool full_run = K_ >= 128 && e2_row < kdim && v0 + e2_c0 + kNState <= vdim;
         if constexpr (kVecState) {
-            if (p.h0 && p.h0_sv == 1) {
-                const int64_t at = si.n * p.h0_sn + hv * p.h0_sh + (32 * q + lane) * p.h0_sk + v0 + cbase;
+            if (p.h0 && p.h0_sv == 1 && full_run) {
+                const int64_t at = si.n * p.h0_sn + hv * p.h0_sh + e2_row * p.h0_sk + v0 + e2_c0;
                 h0_run = reinterpret_cast<const uint8_t*>(p.h0) + at * static_cast<int64_t>(h0_esz);
                 if (reinterpret_cast<uintptr_t>(h0_run) & 15) h0_run = nullptr;
             }
@@ -382,22 +413,22 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
                 int row, col;
                 st_row_col(i, row, col);
                 float x = 0.0f;
-                if (p.h0)
+                if (p.h0 && row < kdim && v0 + col < vdim)
                     x = load_io(p.h0, p.h0_dtype, si.n * p.h0_sn + hv * p.h0_sh + row * p.h0_sk + (v0 + col) * p.h0_sv);
                 st[i] = ref ? round_bf16(x) : x;
             }
         }
         auto write_state_tile = [&]() {
-            if constexpr (K_ == 128) {
-                const int row = 32 * q + lane;
+            if constexpr (K_ >= 128) {
+                const int row = e2_row;
 #pragma unroll
-                for (int j = 0; j < Cfg::kCW / 8; ++j) {
+                for (int j = 0; j < Cfg::kE2Cols / 8; ++j) {
                     uint4 v;
                     v.x = pack_bf16x2(st[8 * j + 0], st[8 * j + 1]);
                     v.y = pack_bf16x2(st[8 * j + 2], st[8 * j + 3]);
                     v.z = pack_bf16x2(st[8 * j + 4], st[8 * j + 5]);
                     v.w = pack_bf16x2(st[8 * j + 6], st[8 * j + 7]);
-                    *reinterpret_cast<uint4*>(s_tile + tile_off<Cfg::kSw64>(row, cbase + 8 * j, Cfg::kSSubBytes)) = v;
+                    *reinterpret_cast<uint4*>(s_tile + tile_off<Cfg::kSw64>(row, e2_c0 + 8 * j, Cfg::kSSubBytes)) = v;
                 }
             } else {
 #pragma unroll
@@ -409,16 +440,21 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
                 }
             }
         };
+        // h rows this warp stores, and the columns (within the V tile) of its sub-tiles
+        const int h_r0 = (K_ >= 128) ? e2_row - lane : Cfg::kHRows * q;
+        const int h_c0 = (K_ >= 128) ? e2_c0 : cbase;
+        const int h_nc = (K_ >= 128) ? Cfg::kE2Cols : Cfg::kCW;
         auto store_h = [&](int64_t chunk) {
-            // this warp's rows of its sub-tiles -> h[b, boh+chunk, hv, rows, cols]
+            // this warp's rows of its sub-tiles -> h[b, boh+chunk, hv, rows, cols]; boxes that
+            // lie wholly past K or V are skipped, partial ones are clipped by the tensor map
             if (lane == 0) {
 #pragma unroll
                 for (int sub = 0; sub < Cfg::kSubV; ++sub) {
-                    if (sub * Cfg::kSubCols < cbase || sub * Cfg::kSubCols >= cbase + Cfg::kCW) continue;
-                    tma_store_5d(&args.maps.h, s_tile + sub * Cfg::kSSubBytes + Cfg::kHRows * q * Cfg::kRowB,
-                                 v0 + sub * Cfg::kSubCols,
-                                 Cfg::kHRows * q, static_cast<int>(hv), static_cast<int>(si.boh + chunk),
-                                 static_cast<int>(si.b));
+                    if (sub * Cfg::kSubCols < h_c0 || sub * Cfg::kSubCols >= h_c0 + h_nc) continue;
+                    if (h_r0 >= kdim || v0 + sub * Cfg::kSubCols >= vdim) continue;
+                    tma_store_5d(&args.maps.h, s_tile + sub * Cfg::kSSubBytes + h_r0 * Cfg::kRowB,
+                                 v0 + sub * Cfg::kSubCols, h_r0, static_cast<int>(hv),
+                                 static_cast<int>(si.boh + chunk), static_cast<int>(si.b));
                 }
                 bulk_commit_group();
             }
@@ -428,6 +464,7 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
         // Pack v_new after MMA2 is released (64-column tiles); the 10-warp 128-column
         // configuration packs it with v_decay to stay within its register budget.
         constexpr bool kDeferVnew = VT <= 64;
+        const uint32_t vo_base = Cfg::kSplitVout ? static_cast<uint32_t>(e * Cfg::kVoutRegion) : 0u;
 
         bool ok = true;
         write_state_tile();
@@ -576,9 +613,9 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
                 for (int i = 0; i < kPairs; ++i) {
                     const int cb = i >> 3, j = (i >> 1) & 3, half = i & 1;
                     const int t = half ? tb : ta;
-                    if (t < len) {
-                        const int64_t vi = si.b * p.v_sb + (t0 + t) * p.v_st + hv * p.v_sh + v0 + cbase + 32 * cb +
-                                           8 * j + pc;
+                    const int col = cbase + 32 * cb + 8 * j + pc;  // even, and V % 8 == 0: col < V covers the pair
+                    if (t < len && v0 + col < vdim) {
+                        const int64_t vi = si.b * p.v_sb + (t0 + t) * p.v_st + hv * p.v_sh + v0 + col;
                         *reinterpret_cast<uint32_t*>(reinterpret_cast<__nv_bfloat16*>(p.v_new) + vi) = vos[i];
                     }
                 }
@@ -586,16 +623,33 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
                 // staging free: the store of chunk c-1 is read (only h[c]'s may be pending)
                 if (lane == 0) bulk_wait_group_read1();
                 __syncwarp();
+                if constexpr (Cfg::kSplitVout) {
 #pragma unroll
-                for (int i = 0; i < kPairs; ++i) *reinterpret_cast<uint32_t*>(vout + offs[i]) = vos[i];
+                    for (int i = 0; i < kPairs; ++i) {
+                        const int j = (i >> 1) & 3, half = i & 1;
+                        *reinterpret_cast<uint32_t*>(vout + vo_base + tile_off<true>(half ? tb : ta, 8 * j + pc, 0)) =
+                            vos[i];
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < kPairs; ++i) *reinterpret_cast<uint32_t*>(vout + offs[i]) = vos[i];
+                }
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) {
+                    if constexpr (Cfg::kSplitVout) {
+                        if (v0 + cbase < vdim)
+                            tma_store_4d(&args.maps.v, vout + vo_base + 16 * q * 64, v0 + cbase, static_cast<int>(hv),
+                                         static_cast<int>(t0 + 16 * q), static_cast<int>(si.b));
+                    } else {
 #pragma unroll
-                    for (int sub = 0; sub < Cfg::kSubV; ++sub) {
-                        if (sub * Cfg::kSubCols < cbase || sub * Cfg::kSubCols >= cbase + Cfg::kCW) continue;
-                        tma_store_4d(&args.maps.v, vout + sub * Cfg::kUSub + 16 * q * Cfg::kRowB, v0 + sub * Cfg::kSubCols,
-                                     static_cast<int>(hv), static_cast<int>(t0 + 16 * q), static_cast<int>(si.b));
+                        for (int sub = 0; sub < Cfg::kSubV; ++sub) {
+                            if (sub * Cfg::kSubCols < cbase || sub * Cfg::kSubCols >= cbase + Cfg::kCW) continue;
+                            if (v0 + sub * Cfg::kSubCols >= vdim) continue;
+                            tma_store_4d(&args.maps.v, vout + sub * Cfg::kUSub + 16 * q * Cfg::kRowB,
+                                         v0 + sub * Cfg::kSubCols, static_cast<int>(hv), static_cast<int>(t0 + 16 * q),
+                                         static_cast<int>(si.b));
+                        }
                     }
                     bulk_commit_group();
                 }
@@ -616,10 +670,10 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
                 }
                 __syncwarp();
             };
-            if constexpr (K_ == 128) {
-                const uint32_t ta2 = tmem + VT + ((32u * q) << 16) + static_cast<uint32_t>(cbase);
+            if constexpr (K_ >= 128) {
+                const uint32_t ta2 = tmem + VT * (1 + (K_ == 256 ? e : 0)) + ((32u * q) << 16) + static_cast<uint32_t>(e2_c0);
 #pragma unroll
-                for (int cb = 0; cb < Cfg::kCW / 32; ++cb) {
+                for (int cb = 0; cb < Cfg::kE2Cols / 32; ++cb) {
                     uint32_t r[2][16];
                     tmem_ld_32x32b_x16(ta2 + 32 * cb, r[0]);
                     tmem_ld_32x32b_x16(ta2 + 32 * cb + 16, r[1]);
@@ -685,8 +739,8 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
         if (ok && p.final_state) {
             uint8_t* f_run = nullptr;
             if constexpr (kVecState) {
-                if (p.f_sv == 1) {
-                    const int64_t at = si.n * p.f_sn + hv * p.f_sh + (32 * q + lane) * p.f_sk + v0 + cbase;
+                if (p.f_sv == 1 && full_run) {
+                    const int64_t at = si.n * p.f_sn + hv * p.f_sh + e2_row * p.f_sk + v0 + e2_c0;
                     f_run = reinterpret_cast<uint8_t*>(p.final_state) + at * (p.f_dtype == kBF16 ? 2 : 4);
                     if (reinterpret_cast<uintptr_t>(f_run) & 15) f_run = nullptr;
                 }
@@ -706,8 +760,9 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
                 for (int i = 0; i < kNState; ++i) {
                     int row, col;
                     st_row_col(i, row, col);
-                    store_io(p.final_state, p.f_dtype, si.n * p.f_sn + hv * p.f_sh + row * p.f_sk + (v0 + col) * p.f_sv,
-                             st[i]);
+                    if (row < kdim && v0 + col < vdim)
+                        store_io(p.final_state, p.f_dtype,
+                                 si.n * p.f_sn + hv * p.f_sh + row * p.f_sk + (v0 + col) * p.f_sv, st[i]);
                 }
             }
         }

@@ -116,7 +116,8 @@ typedef struct {
                                         32<=K==V<=256, N<=4 limits
                                         (infershape.cpp:196-275) */
     int32_t force_kernel;            /* 0 auto, 1 tensor-core path, 2 general path */
-    int32_t v_tile;                  /* 0 auto; else 32 (K = 128 only), 64 or 128 */
+    int32_t v_tile;                  /* 0 auto; else 32 (64 < K <= 128 only), 64 or
+                                        128 (64 only for K > 128) */
     int32_t wait_timeout_ms;         /* 0 = default (2000 ms): bound on every
                                         device-side wait before the kernel
                                         gives up and flags DEVICE_ERROR */
@@ -214,8 +215,10 @@ cgdrStatus cgdrReadDeviceStatus(const void* workspace, uint64_t workspace_size, 
  *   8 bytes per sequence, so up to roughly 8000 sequences fit).
  * - Device: the buffer of the current device is used; `stream` must belong
  *   to it.  The first call on each device looks up the buffer's address
- *   (cudaGetSymbolAddress) with that device current; make that first call
- *   before any stream capture.
+ *   (cudaGetSymbolAddress) with that device current and keeps it for the life
+ *   of the process; make that first call before any stream capture, and do
+ *   not reset the device (cudaDeviceReset) between calls, since a reset
+ *   invalidates the kept address.  Device ordinals up to 63 are served.
  * - Sharing: every call shares the one buffer, which keeps the last call's
  *   contents; each call clears its status word before its kernels run.
  *   Calls whose work overlaps on the GPU (other streams, other host

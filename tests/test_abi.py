@@ -118,8 +118,10 @@ def test_rejects_out_of_range_head_dimension():
     d["initial_state"] = e((2, 8, 16, 16))
     d["h"], d["v"], d["final_state"] = e((1, 8, 158, 16, 16)), e((1, 8, 10016, 16)), e((2, 8, 16, 16))
     reject(d, "BAD_SHAPE")
-    # outside the reference's limits this build still accepts K = V = 16 (general kernel)
-    assert phase1(d, strict=False).plan["kernel"] == 2
+    # outside the reference's limits this build still accepts K = V = 16 (tensor cores,
+    # K tile 64 with the columns past K zero-filled by the tensor maps)
+    pl = phase1(d, strict=False).plan
+    assert pl["kernel"] == 1 and pl["v_tile"] == 64 and pl["v_tile_count"] == 1
 
 
 def test_rejects_non_divisible_head_ratio():
@@ -211,7 +213,7 @@ def test_plan_rejects_half_present_varlen_metadata():
 
 
 def test_plan_kernel_selection():
-    """bf16 with K in {64, 128} and V % 64 == 0 -> tensor cores; else general."""
+    """bf16 with K, V multiples of 8 and K <= 256 -> tensor cores; else general."""
     B, T, H = 4, 8192, 32
     k, w, u, g = e((B, T, H, 128)), e((B, T, H, 128)), e((B, T, H, 128)), e((B, T, H), F32)
     h, v, f = e((B, 128, H, 128, 128)), e((B, T, H, 128)), e((B, H, 128, 128), F32)
@@ -230,6 +232,43 @@ def test_plan_kernel_selection():
         cg.ChunkGatedDeltaRuleFwdH(k32, w32, u32, e((1, 256, 2), F32), None, None, None, 64,
                                    e((1, 4, 2, 64, 64), F32), e((1, 256, 2, 64), F32), None,
                                    layout="token_major", numerics="reference")
+
+
+@pytest.mark.parametrize("K,V,vt,tiles,block", [
+    (32, 32, 64, 1, 192),     # K tile 64, one partial V tile
+    (64, 96, 64, 2, 192),     # K tile 64, partial second V tile
+    (96, 96, 32, 3, 192),     # K tile 128, 32-column tiles
+    (128, 40, 32, 2, 192),    # V % 32 != 0: partial 32-column tile
+    (256, 256, 64, 4, 320),   # K tile 256: two M = 128 halves of MMA2, 8 epilogue warps
+    (200, 64, 64, 1, 320),
+])
+def test_plan_tensor_core_head_widths(K, V, vt, tiles, block):
+    """The reference accepts 32 <= K == V <= 256 (infershape.cpp:214-219); every K, V
+    that is a multiple of 8 up to 256 runs on the tensor cores, in a K tile of 64,
+    128 or 256 and V tiles clipped at V."""
+    B, T, H = 1, 200, 2
+    op = cg.ChunkGatedDeltaRuleFwdH(e((B, T, H, K)), e((B, T, H, K)), e((B, T, H, V)), e((B, T, H), F32), None,
+                                    None, None, 64, e((B, 4, H, K, V)), e((B, T, H, V)), e((B, H, K, V), F32),
+                                    layout="token_major", numerics="fp32_state")
+    pl = op.plan
+    assert pl["kernel"] == 1, pl
+    assert (pl["v_tile"], pl["v_tile_count"], pl["block"]) == (vt, tiles, block)
+    assert pl["task_count"] == B * H * tiles
+    # widths that are not multiples of 8 stay on the general kernel
+    if K == 32:
+        op = cg.ChunkGatedDeltaRuleFwdH(e((B, T, H, 36)), e((B, T, H, 36)), e((B, T, H, 36)), e((B, T, H), F32),
+                                        None, None, None, 64, e((B, 4, H, 36, 36)), e((B, T, H, 36)),
+                                        e((B, H, 36, 36), F32), layout="token_major", numerics="fp32_state")
+        assert op.plan["kernel"] == 2
+
+
+def test_plan_rejects_unbuilt_tile_choices():
+    B, T, H = 1, 128, 2
+    args = lambda K, V: (e((B, T, H, K)), e((B, T, H, K)), e((B, T, H, V)), e((B, T, H), F32), None, None,  # noqa: E731
+                         None, 64, e((B, 2, H, K, V)), e((B, T, H, V)), None)
+    for K, vt in ((256, 128), (64, 32)):
+        with pytest.raises(cg.CgdrError, match="UNSUPPORTED"):
+            cg.ChunkGatedDeltaRuleFwdH(*args(K, K), layout="token_major", numerics="fp32_state", v_tile=vt)
 
 
 def test_executor_lifecycle_and_errors():

@@ -68,8 +68,6 @@ def test_golden_reference_numerics(case, kernel):
     """run() (head-major layout, reference rounding) against run_reference."""
     dev = _cuda()
     spec, inp, gold = cases.load_case(case)
-    if kernel == "tc" and spec["dim"] not in (64, 128):
-        pytest.skip("tensor-core path covers K = V in {64, 128}")
     t = _to_dev(inp, dev)
     h, v, f = cg.run(t["k"], t["w"], t["u"], t["g"], t.get("initial_state"), t["cu_seqlens"],
                      t["chunk_indices"], 64, force_kernel=1 if kernel == "tc" else 2, check_device_status=True)
@@ -423,3 +421,30 @@ def test_value_width_multiple_of_32(V):
     oh, ov, of = H.oracle_run(inp, "fp32_state")
     H.assert_close(h, oh, BF_TOL, BF_TOL, f"V{V}/h fp32")
     H.assert_close(f, of, BF_TOL, BF_TOL, f"V{V}/final fp32")
+
+
+@pytest.mark.parametrize("K,V", [(32, 32), (96, 96), (256, 256), (48, 40), (64, 96), (200, 64), (128, 40)])
+@pytest.mark.parametrize("varlen", [False, True])
+def test_head_widths_on_tensor_cores(K, V, varlen):
+    """The reference accepts 32 <= K == V <= 256 (infershape.cpp:214-219).  On the
+    tensor cores K runs in a tile of 64, 128 or 256 (k_c and w_c zero-filled past K,
+    K = 256 with MMA2 as two M = 128 halves) and V tiles are clipped at V.  Both
+    arithmetic modes against the oracle at the north-star tolerance, the reference
+    rounding chain >= 99 % bit-equal, and the general kernel agreeing."""
+    dev = _cuda()
+    if varlen:
+        inp = H.make_inputs(1, 450, 4, K, V, HK=2, seed=K + V, cu_seqlens=[0, 130, 131, 300, 450])
+    else:
+        inp = H.make_inputs(2, 333, 4, K, V, HK=2, seed=K + V)
+    for numerics in ("fp32_state", "reference"):
+        h, v, f = _run_fla(inp, dev, numerics=numerics, force_kernel=1)
+        oh, ov, of = H.oracle_run(inp, numerics, final_dtype="f32")
+        H.assert_close(h, oh, BF_TOL, BF_TOL, f"K{K} V{V} {numerics}/h")
+        H.assert_close(v, ov, BF_TOL, BF_TOL, f"K{K} V{V} {numerics}/v")
+        H.assert_close(f, of, BF_TOL, BF_TOL, f"K{K} V{V} {numerics}/final")
+        if numerics == "reference":
+            for got, ref in ((h, oh), (v, ov)):
+                assert np.mean(H.to_bits(got) == ref) >= 0.99
+        gh, gv, gf = _run_fla(inp, dev, numerics=numerics, force_kernel=2)
+        H.assert_close(h, gh, BF_TOL, BF_TOL, f"K{K} V{V} {numerics}/h tc vs general")
+        H.assert_close(f, gf, BF_TOL, BF_TOL, f"K{K} V{V} {numerics}/final tc vs general")

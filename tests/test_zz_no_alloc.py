@@ -6,8 +6,9 @@ pool owns the device memory, or a latency-critical path that must not take
 cudaMalloc's implicit device synchronisation.  For them the library runs
 the op on a 64 KiB scratch buffer compiled into it instead of a caller
 workspace.  These tests call that entry point through the C ABI and check
-it against the ordinary workspace entry point, twice in a row (the buffer is
-shared by every call and keeps the previous call's contents).
+it against the ordinary workspace entry point and the CPU oracle, in both
+arithmetic modes, on calls in a row whose plans differ (the buffer is shared
+by every call and keeps the previous call's contents).
 
 This file is collected last so that a run stopping at its first failure has
 already run every other test.
@@ -51,23 +52,23 @@ def _outputs(t, cu):
     return ci, h, v, f
 
 
-def _plan(t, cu, ci, h, v, f):
+def _plan(t, cu, ci, h, v, f, numerics):
     return cg.ChunkGatedDeltaRuleFwdH(t["k"], t["w"], t["u"], t["g"], t["initial_state"], cu, ci, 64, h, v, f,
-                                      layout="token_major", numerics="fp32_state")
+                                      layout="token_major", numerics=numerics)
 
 
-def _run_workspace(t, cu):
+def _run_workspace(t, cu, numerics):
     ci, h, v, f = _outputs(t, cu)
-    op = _plan(t, cu, ci, h, v, f)
+    op = _plan(t, cu, ci, h, v, f, numerics)
     ws = torch.empty(max(op.workspace_size, 256), dtype=torch.uint8, device=t["k"].device)
     op(ws)
     return h, v, f
 
 
-def _run_no_alloc(t, cu):
+def _run_no_alloc(t, cu, numerics):
     lib = _lib.load()
     ci, h, v, f = _outputs(t, cu)
-    op = _plan(t, cu, ci, h, v, f)
+    op = _plan(t, cu, ci, h, v, f, numerics)
     assert op.workspace_size <= _lib.NOALLOC_SCRATCH_BYTES
     ex, op._ex = op._ex, None  # the entry point consumes the executor
     status = ctypes.c_int32(-1)
@@ -78,22 +79,34 @@ def _run_no_alloc(t, cu):
     return h, v, f
 
 
-@pytest.mark.parametrize("varlen", [False, True])
-def test_no_alloc_entry_matches_workspace_entry(varlen):
-    dev = _cuda()
-    if varlen:
+def _case(which, dev):
+    if which == "varlen4":
         inp = H.make_inputs(1, 700, 4, 128, 128, seed=21, cu_seqlens=[0, 5, 200, 333, 700])
+    elif which == "varlen2":
+        inp = H.make_inputs(1, 400, 4, 64, 64, seed=22, cu_seqlens=[0, 129, 400])
     else:
         inp = H.make_inputs(2, 300, 4, 128, 128, seed=23)
-    t = {n: (x.to(dev) if isinstance(x, torch.Tensor) else x) for n, x in inp.items()}
-    cu = t.get("cu_seqlens")
-    ref = _run_workspace(t, cu)
-    for _ in range(2):  # two calls in a row on the shared buffer
-        got = _run_no_alloc(t, cu)
+    return inp, {n: (x.to(dev) if isinstance(x, torch.Tensor) else x) for n, x in inp.items()}
+
+
+@pytest.mark.parametrize("numerics", ["fp32_state", "reference"])
+def test_no_alloc_entry_matches_workspace_entry(numerics):
+    """Calls in a row with plans that leave different metadata in the shared
+    buffer (4 sequences, fixed length, 2 sequences, then 4 again): each result
+    equals the workspace entry's bit for bit and is within the north-star
+    tolerance of the CPU oracle."""
+    dev = _cuda()
+    for which in ("varlen4", "fixed", "varlen2", "varlen4"):
+        inp, t = _case(which, dev)
+        cu = t.get("cu_seqlens")
+        ref = _run_workspace(t, cu, numerics)
+        got = _run_no_alloc(t, cu, numerics)
         torch.cuda.synchronize()
-        for name, a, b in zip(("h", "v_new", "final_state"), got, ref):
-            assert torch.isfinite(a.float()).all(), name
-            H.assert_close(a, b, TOL, TOL, f"no-alloc {name}")
+        oh, ov, of = H.oracle_run(inp, numerics, final_dtype="f32")
+        for name, a, b, o in zip(("h", "v_new", "final_state"), got, ref, (oh, ov, of)):
+            assert torch.isfinite(a.float()).all(), f"{which}/{name}"
+            assert torch.equal(a, b), f"{which}/{name}: no-alloc entry differs from the workspace entry"
+            H.assert_close(a, o, TOL, TOL, f"{which}/{name} vs oracle")
 
 
 def test_no_alloc_rejects_plans_beyond_the_scratch_limit():
