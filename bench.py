@@ -53,6 +53,8 @@ CONFIGS = {
     "nsq": dict(B=1, T=8192, H=32, HK=32, K=128, V=128, scaling="weak"),
     # 16 sequences packed into T=32768 via cu_seqlens (lengths uniform in [64, 4096], multiples of 64)
     "c4": dict(B=1, T=32768, H=32, HK=32, K=128, V=128, scaling="weak", seqs=16),
+    # the widest head the reference accepts (K = V = 256): 32 (sequence, head) pairs x 4 V tiles
+    "w256": dict(B=4, T=8192, H=8, HK=8, K=256, V=256, scaling="weak"),
 }
 
 
@@ -288,6 +290,123 @@ def cpu_reference_rate(c, budget_s, n_threads, max_pairs=None):
     return rate, desc, threads
 
 
+def cpu_parity_check(c, inp, out, numerics, heads=None):
+    """The CPU oracle as the checker of one timed output (outside every timed
+    region): sequence 0 and two heads, against the arithmetic the bench ran and
+    against the reference semantics, at the north-star rtol = atol = 2e-2."""
+    import numpy as np
+    import torch
+    sys.path.insert(0, str(ROOT / "tests"))
+    from oracle import oracle as o  # the checker
+
+    H, HK = c["H"], c["HK"]
+    heads = heads or [0, H - 1]
+    kheads = [hh // (H // HK) for hh in heads]
+    cu = inp.get("cu_seqlens")
+    t0, t1 = (0, c["T"]) if cu is None else (int(cu[0]), int(cu[1]))
+    nc = (t1 - t0 + 63) // 64
+    bits = lambda t: t.contiguous().cpu().view(torch.int16).numpy().view(np.uint16)  # noqa: E731
+    k = bits(inp["k"][0:1, t0:t1, kheads])
+    w = bits(inp["w"][0:1, t0:t1, heads])
+    u = bits(inp["u"][0:1, t0:t1, heads])
+    g = inp["g"][0:1, t0:t1, heads].contiguous().cpu().numpy()
+    h0 = None if inp["initial_state"] is None else inp["initial_state"][0:1, heads].contiguous().cpu().numpy()
+    h, v, f = out
+    got = {"h": h[0:1, 0:nc, heads].float().cpu().numpy(), "v_new": v[0:1, t0:t1, heads].float().cpu().numpy(),
+           "final_state": f[0:1, heads].float().cpu().numpy()}
+
+    def stats(mode):
+        oh, ov, of = o.fwd_h(k, w, u, g, h0, None, mode=mode, final_dtype="f32")
+        ref = {"h": oh, "v_new": ov, "final_state": of}
+        bad = n = 0
+        mx = 0.0
+        for name in ref:
+            r = ref[name]
+            r = (r.astype(np.uint32) << 16).view(np.float32) if r.dtype == np.uint16 else r
+            a = got[name].reshape(-1).astype(np.float64)
+            r = r.reshape(-1).astype(np.float64)
+            err = np.abs(a - r)
+            bad += int((~(err <= 2e-2 + 2e-2 * np.abs(r))).sum())
+            n += a.size
+            mx = max(mx, float(err.max(initial=0.0)))
+        return {"mode": mode, "bad": bad, "n": n, "max_abs": mx}
+
+    res = {"sample": f"sequence 0 (tokens {t0}..{t1}), heads {heads}: h, v_new, final_state",
+           "tolerance": "rtol = atol = 2e-2", "vs_oracle": stats(numerics)}
+    res["bad"], res["n"], res["max_abs"] = res["vs_oracle"]["bad"], res["vs_oracle"]["n"], res["vs_oracle"]["max_abs"]
+    if numerics != "reference":
+        res["vs_reference_semantics"] = stats("reference")
+    return res
+
+
+def time_launches(step, steps, warmup, stream, world):
+    """Device time of `steps` launches of `step` after `warmup`: the mean per
+    launch (CUDA events on the launching stream), max over ranks."""
+    import torch
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * steps)]
+    for i in range(steps):
+        ev[2 * i].record(stream)
+        step()
+        ev[2 * i + 1].record(stream)
+    torch.cuda.synchronize()
+    ms = sum(ev[2 * i].elapsed_time(ev[2 * i + 1]) for i in range(steps)) / steps
+    return max_over_ranks(ms, world)
+
+
+def strong_scaling_leg(args, world, rank, dev, stream):
+    """The benchmark's multi-GPU configuration (B=8, T=8192, H=64, K=128, V=256)
+    with its value heads split over the ranks (no collective on the data path),
+    timed after the headline and outside its timed region.  Rank 0 also times the
+    whole configuration on its own GPU, so that one run gives both ends of the
+    strong-scaling curve."""
+    import torch
+    import cann_operator_challenge_august_b200 as cg
+    full = CONFIGS["c5"]
+    c = shard(full, world, rank)
+    opts = dict(numerics=args.numerics)
+
+    def run(cfg, seed):
+        inp = gen_inputs(cfg, seed=seed, device=dev)
+        step = lambda: cg.chunk_gated_delta_rule_fwd_h(inp["k"], inp["w"], inp["u"], inp["g"],  # noqa: E731
+                                                      inp["initial_state"], **opts)
+        return inp, step
+
+    inp, step = run(c, 2000 + rank)
+    ms_n = time_launches(step, args.steps, args.warmup, stream, world)
+    del inp, step
+    torch.cuda.empty_cache()
+    ms_1 = ms_n
+    if world > 1:
+        t = 0.0
+        if rank == 0:
+            inp, step = run(full, 2000)
+            t = time_launches(step, args.steps, args.warmup, stream, 1)
+            del inp, step
+            torch.cuda.empty_cache()
+        ms_1 = max_over_ranks(t, world)
+    peak, _ = load_peaks()
+    shard_bytes = config_bytes(c, 2000)
+    full_bytes = config_bytes(full, 2000)
+    tokens = full["B"] * full["T"]
+    return {
+        "config": (f"c5: B={full['B']} T={full['T']} H={full['H']} K={full['K']} V={full['V']}, "
+                   f"{c['H']} value heads per rank, no collective on the data path"),
+        "ranks": world,
+        "ms_per_launch": ms_n,
+        "tokens_per_s": tokens / (ms_n / 1000.0),
+        "hbm_gbs_per_gpu": shard_bytes / (ms_n / 1000.0) / 1e9,
+        "roofline_frac_per_gpu": shard_bytes / (ms_n / 1000.0) / 1e9 / peak,
+        "one_gpu_ms_per_launch": ms_1,
+        "one_gpu_roofline_frac": full_bytes / (ms_1 / 1000.0) / 1e9 / peak,
+        "speedup_vs_one_gpu": ms_1 / ms_n,
+        "efficiency_vs_one_gpu": ms_1 / ms_n / world,
+    }
+
+
 def run_reference_arm(args, cfg_name, c, world, rank):
     if rank != 0:
         return 0
@@ -365,6 +484,9 @@ def main() -> int:
                     help="--op gdr: the recurrence and output kernels (default: the planner's choice)")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-parity", action="store_true", help="skip the oracle check of the timed output")
+    ap.add_argument("--no-strong-scaling", action="store_true",
+                    help="skip the head-sharded multi-GPU configuration after the headline")
     ap.add_argument("--op", choices=["fwd_h", "chunk_o", "wy", "gdr"], default="fwd_h",
                     help="fwd_h: the recurrence (the headline); chunk_o: the chunk output that consumes it; "
                          "wy: the WY representation that feeds it; gdr: the whole forward operator")
@@ -434,6 +556,11 @@ def main() -> int:
     tokens_per_step = c["B"] * c["T"] * world
     value = tokens_per_step / (ms_per_step / 1000.0)
 
+    # ---- the last timed output, checked against the CPU oracle (rank 0, untimed)
+    parity = None
+    if rank == 0 and not args.no_parity:
+        parity = cpu_parity_check(c, inp, out, args.numerics)
+
     # ---- e2e: public API with pinned host buffers, copies inside the timed region
     host = {n: (x.cpu().pin_memory() if x is not None else None) for n, x in inp.items()}
     # bytes the front end copies to the device (cu_seqlens is read on the host; the chunk
@@ -469,6 +596,11 @@ def main() -> int:
     if "chunk_indices" in inp:
         assert sum((L + 63) // 64 for L in varlen_lengths(c["seqs"], c["T"], 1000 + rank)) == inp["chunk_indices"].shape[0]
     peak, peak_kind = load_peaks()
+
+    # ---- head-sharded multi-GPU configuration (strong scaling), after everything above
+    strong = None
+    if not args.no_strong_scaling and args.config == "ns" and CONFIGS["c5"]["H"] % world == 0:
+        strong = strong_scaling_leg(args, world, rank, dev, stream)
     achieved = nbytes / (per_launch_ms / 1000.0) / 1e9
     plan = cg.ChunkGatedDeltaRuleFwdH(inp["k"], inp["w"], inp["u"], inp["g"], inp["initial_state"],
                                       inp.get("cu_seqlens"), inp.get("chunk_indices"), 64,
@@ -497,7 +629,7 @@ def main() -> int:
             "data": "synthetic (seeded, generated on device per rank)",
             "numerics": args.numerics,
             "config": config_block(args.config, c, world, nbytes),
-            "gpu_launches": args.steps,
+            "gpu_launches": args.steps * (2 if "cu_seqlens" in inp else 1),
             "roofline": {
                 "bound": "hbm",
                 "achieved": achieved,
@@ -513,8 +645,12 @@ def main() -> int:
             "hbm_gbs_per_gpu": achieved,
             "clocks": clk,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "ms_per_step": e2e_ms},
+                    "ms_per_step": e2e_ms,
+                    "copy_gbs_per_rank": None if e2e_ms is None else (h2d + d2h) / (e2e_ms / 1000.0) / 1e9,
+                    "copy_gbs_total": None if e2e_ms is None else world * (h2d + d2h) / (e2e_ms / 1000.0) / 1e9},
             "cpu_baseline": cpu,
+            "parity": parity,
+            "strong_scaling": strong,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
