@@ -2,12 +2,15 @@
 golden vectors and the CPU oracle.
 
 Tolerances:
-* reference numerics (the contest's rounding chain) against goldens made by
-  the reference's own run_reference: at least 97% of elements bit-equal and
-  at least 99.9% within the north-star rtol/atol of 2e-2 -- the residue is
-  fp32 summation order flipping a bf16 rounding of the bf16 state, which
-  then propagates through slowly decaying chunks (the C oracle differs from
-  the goldens the same way);
+* both arithmetic modes against goldens made by the reference's own
+  run_reference, per case, kernel and output: no more elements beyond the
+  north-star rtol/atol of 2e-2, and no larger maximum difference, than the
+  budget recorded from a B200 run (tests/golden/parity_budget.json, written by
+  tests/golden/make_parity_budget.py).  The reference rounding chain keeps at
+  least 97% of elements bit-equal; its residue is fp32 summation order
+  flipping a bf16 rounding of the bf16 state.  The fp32-state arithmetic
+  differs from the goldens only where the goldens' own rounding error is
+  largest (tests/test_accuracy.py compares both with a float64 evaluation);
 * fp32-state numerics on the benchmark recipes: rtol/atol 2e-2 against the
   reference semantics (the north-star bar) and against the fp32-state oracle;
 * fp32 I/O: rtol/atol 1e-4 against the fp32-state oracle (fp64 sums).
@@ -15,12 +18,15 @@ Tolerances:
 
 from __future__ import annotations
 
+import json
+
 import numpy as np
 import pytest
 import torch
 
 import cases
 import helpers as H
+import make_parity_budget as PB
 
 pytestmark = pytest.mark.gpu
 
@@ -28,6 +34,8 @@ cg = pytest.importorskip("cann_operator_challenge_august_b200")
 
 MAN = cases.load_manifest()
 GOLDEN = list(MAN["cases"])
+_BUDGET_PATH = cases.GOLDEN_DIR / "parity_budget.json"
+BUDGET = json.loads(_BUDGET_PATH.read_text()) if _BUDGET_PATH.exists() else None
 BF_TOL = 2e-2
 F32_TOL = 1e-4
 
@@ -45,19 +53,23 @@ def _to_dev(inp, dev):
     return out
 
 
-def _golden_check(name, out_name, got, gold, min_exact=0.97, max_bad_frac=1e-3):
-    bits = H.to_bits(got).reshape(-1)
-    if "samples" in gold:
-        idx, ref = gold["samples"][out_name]
-        bits = bits[idx]
-    else:
-        ref = gold[out_name].reshape(-1)
-    exact = float(np.mean(bits == ref)) if bits.size else 1.0
-    st = H.close_stats(bits, ref, BF_TOL, BF_TOL)
-    assert exact >= min_exact, f"{name}/{out_name}: only {exact:.4%} bit-equal; {st}"
-    assert st["bad"] <= max(0, int(max_bad_frac * st["n"])), f"{name}/{out_name}: {st}"
-    assert st["max_abs"] <= 0.125, f"{name}/{out_name}: {st}"
-    return exact
+def _golden_check(case, name, bits, gold, numerics, kernel, min_exact=None):
+    """Elements beyond 2e-2 of the golden and the largest difference, against the
+    case's recorded budget."""
+    assert BUDGET is not None, "tests/golden/parity_budget.json is missing (run tests/golden/make_parity_budget.py)"
+    bad, mx = PB.measure(gold, name, bits)
+    lim_bad, lim_max = BUDGET[numerics][kernel][case][name]
+    assert bad <= lim_bad, f"{case}/{name} ({numerics}, {kernel}): {bad} elements beyond 2e-2, budget {lim_bad}"
+    assert mx <= lim_max + 1e-6, f"{case}/{name} ({numerics}, {kernel}): max |diff| {mx}, budget {lim_max}"
+    if min_exact is not None:
+        a = np.ascontiguousarray(bits).reshape(-1)
+        if "samples" in gold:
+            idx, ref = gold["samples"][name]
+            a = a[idx]
+        else:
+            ref = gold[name].reshape(-1)
+        exact = float(np.mean(a == ref)) if a.size else 1.0
+        assert exact >= min_exact, f"{case}/{name}: only {exact:.4%} bit-equal"
 
 
 # ---------------------------------------------------------------- golden vectors
@@ -74,13 +86,14 @@ def test_golden_reference_numerics(case, kernel):
     torch.cuda.synchronize()
     for n, out in (("h", h), ("v", v), ("final_state", f)):
         assert list(out.shape) == gold["shapes"][n]
-        _golden_check(case, n, out, gold)
+        _golden_check(case, n, H.to_bits(out), gold, "reference", kernel, min_exact=0.97)
 
 
+@pytest.mark.parametrize("kernel", ["tc", "general"])
 @pytest.mark.parametrize("case", GOLDEN)
-def test_golden_fp32_state_numerics(case):
-    """fla front end, fp32-state arithmetic, against the fp32-state oracle
-    (2e-2), and its distance to the reference goldens stays small."""
+def test_golden_fp32_state_numerics(case, kernel):
+    """fla front end, fp32-state arithmetic: within 2e-2 of the fp32-state oracle
+    everywhere, and within its recorded budget of the reference goldens."""
     dev = _cuda()
     spec, inp, gold = cases.load_case(case)
     t = _to_dev(inp, dev)
@@ -88,23 +101,18 @@ def test_golden_fp32_state_numerics(case):
     u = t["u"].transpose(1, 2).contiguous()
     g = t["g"].transpose(1, 2).contiguous()
     h, v, f = cg.chunk_gated_delta_rule_fwd_h(t["k"], w, u, g, t.get("initial_state"), cu_seqlens=t["cu_seqlens"],
-                                              chunk_indices=t["chunk_indices"], check_device_status=True)
+                                              chunk_indices=t["chunk_indices"], check_device_status=True,
+                                              force_kernel=1 if kernel == "tc" else 2,
+                                              final_state_dtype=torch.bfloat16)
     wn, un, gn = H.hm_to_tm_inputs(inp["w"], inp["u"], inp["g"])
-    oh, ov, of = H.oracle.fwd_h(inp["k"], wn, un, gn, inp.get("initial_state"), inp["cu_seqlens"], mode="fp32_state")
+    oh, ov, of = H.oracle.fwd_h(inp["k"], wn, un, gn, inp.get("initial_state"), inp["cu_seqlens"], mode="fp32_state",
+                                final_dtype="bf16")
     H.assert_close(h, oh, BF_TOL, BF_TOL, f"{case}/h")
     H.assert_close(v, ov, BF_TOL, BF_TOL, f"{case}/v")
     H.assert_close(f, of, BF_TOL, BF_TOL, f"{case}/final")
-    # distance to the reference rounding chain: bounded, few elements past 2e-2
     hh, vv = H.tm_to_hm_outputs(H.to_bits(h), H.to_bits(v))
-    for n, a in (("h", hh), ("v", vv)):
-        a = a.reshape(-1)
-        if "samples" in gold:
-            idx, ref = gold["samples"][n]
-            a = a[idx]
-        else:
-            ref = gold[n].reshape(-1)
-        st = H.close_stats(a, ref, BF_TOL, BF_TOL)
-        assert st["bad"] <= 0.01 * st["n"] and st["max_abs"] <= 0.125, f"{case}/{n}: {st}"
+    for n, a in (("h", hh), ("v", vv), ("final_state", H.to_bits(f))):
+        _golden_check(case, n, a, gold, "fp32_state", kernel)
 
 
 # ---------------------------------------------------------------- benchmark configs

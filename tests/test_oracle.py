@@ -103,3 +103,22 @@ def test_oracle_edge_semantics():
     assert np.array_equal(H.as_f32(h[0, 0]), H.as_f32(H.oracle.f32_to_bf16_bits(h0[0])))
     assert h.shape[1] == 1 + 0 + 2
     assert isinstance(inp["k"], torch.Tensor)
+
+
+def test_parity_budget_covers_every_golden_case():
+    """The per-case budgets the GPU parity tests enforce (written from a B200 run
+    by tests/golden/make_parity_budget.py) cover every golden case, both
+    kernels and both arithmetic modes; the reference rounding chain stays
+    within a handful of elements per case."""
+    import json
+    budget = json.loads((cases.GOLDEN_DIR / "parity_budget.json").read_text())
+    for numerics in ("reference", "fp32_state"):
+        for kernel in ("tc", "general"):
+            table = budget[numerics][kernel]
+            assert set(table) == set(GOLDEN), (numerics, kernel)
+            for case, outs in table.items():
+                assert set(outs) == {"h", "v", "final_state"}
+                for name, (bad, mx) in outs.items():
+                    assert 0 <= bad and 0.0 <= mx <= 0.0625, (numerics, kernel, case, name)
+                    if numerics == "reference":
+                        assert bad <= 2, (kernel, case, name, bad)
