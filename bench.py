@@ -55,6 +55,8 @@ CONFIGS = {
     "c4": dict(B=1, T=32768, H=32, HK=32, K=128, V=128, scaling="weak", seqs=16),
     # the widest head the reference accepts (K = V = 256): 32 (sequence, head) pairs x 4 V tiles
     "w256": dict(B=4, T=8192, H=8, HK=8, K=256, V=256, scaling="weak"),
+    # a quarter of it (one sequence per head): the small case of ncu captures
+    "w256q": dict(B=1, T=8192, H=8, HK=8, K=256, V=256, scaling="weak"),
 }
 
 

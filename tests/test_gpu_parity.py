@@ -195,6 +195,23 @@ def test_config4_varlen():
     inp = H.make_inputs(1, 32768, 32, 128, 128, seed=4, cu_seqlens=cu)
     outs = _run_fla(inp, dev)
     _check_subset(inp, outs, [5, 17], "fp32_state")
+    # within 2e-2 of the reference semantics too
+    _check_subset(inp, outs, [5, 17], "reference")
+
+
+def test_north_star_config():
+    """The headline workload (bf16 B=4 T=8192 H=32 K=V=128, h0 ~ 0.1 randn, final
+    state fp32) as the benchmark runs it: two heads of every sequence against the
+    fp32-state oracle and against the reference semantics at 2e-2, in both
+    arithmetic modes."""
+    dev = _cuda()
+    inp = H.make_inputs(4, 8192, 32, 128, 128, seed=1)
+    for numerics in ("fp32_state", "reference"):
+        outs = _run_fla(inp, dev, numerics=numerics)
+        _check_subset(inp, outs, [0, 31], numerics)
+        if numerics == "fp32_state":
+            _check_subset(inp, outs, [0, 31], "reference")
+        del outs
 
 
 def test_config5_wide_value():
