@@ -247,42 +247,44 @@ def gen_inputs(c, seed, device):
     return out
 
 
+def cpu_sample(c, P, chunks, seed=0):
+    """Seeded inputs of P (sequence, head) pairs x `chunks` chunks of config c, in
+    the oracle's layout (bf16 as uint16 bits), with the benchmark's distributions."""
+    import numpy as np
+    import torch
+    gen = torch.Generator().manual_seed(seed)
+    T = 64 * chunks
+    k = torch.randn(1, T, P, c["K"], generator=gen)
+    k = (k / k.norm(dim=-1, keepdim=True)).to(torch.bfloat16)
+    w = (torch.sigmoid(torch.randn(1, T, P, 1, generator=gen)) * k.float()).to(torch.bfloat16)
+    u = (0.5 * torch.randn(1, T, P, c["V"], generator=gen)).to(torch.bfloat16)
+    g = torch.nn.functional.logsigmoid(torch.randn(1, T, P, generator=gen) + 2.0)
+    g = g.view(1, chunks, 64, P).cumsum(2).view(1, T, P)
+    h0 = 0.1 * torch.randn(1, P, c["K"], c["V"], generator=gen)
+    bits = lambda t: t.contiguous().view(torch.int16).numpy().view(np.uint16)  # noqa: E731
+    return bits(k), bits(w), bits(u), g.numpy(), h0.numpy()
+
+
+def cpu_time(sample, threads):
+    """Seconds of one CPU-oracle run (reference arithmetic) over `sample`."""
+    sys.path.insert(0, str(ROOT / "tests"))
+    from oracle import oracle as o  # the reference arithmetic, restated (timed baseline)
+    t0 = time.perf_counter()
+    o.fwd_h(*sample, mode="reference", n_threads=threads)
+    return time.perf_counter() - t0
+
+
 def cpu_reference_rate(c, budget_s, n_threads, max_pairs=None):
     """Time the CPU oracle (reference arithmetic) on a bounded sample of the
     workload: P (sequence, head) pairs x C chunks.  Returns (tokens/s for the
     whole job, description, threads)."""
-    import numpy as np
-    import torch
-    sys.path.insert(0, str(ROOT / "tests"))
-    from oracle import oracle as o  # the reference arithmetic, restated (timed baseline)
-
     # every host core this process may run on (torchrun sets OMP_NUM_THREADS=1 for its ranks)
     threads = n_threads or len(os.sched_getaffinity(0))
     P = max(1, min(threads, max_pairs or threads, c["B"] * c["H"]))
     NT = (c["T"] + 63) // 64
-    gen = torch.Generator().manual_seed(0)
-
-    def sample(chunks):
-        T = 64 * chunks
-        k = torch.randn(1, T, P, c["K"], generator=gen)
-        k = (k / k.norm(dim=-1, keepdim=True)).to(torch.bfloat16)
-        w = (torch.sigmoid(torch.randn(1, T, P, 1, generator=gen)) * k.float()).to(torch.bfloat16)
-        u = (0.5 * torch.randn(1, T, P, c["V"], generator=gen)).to(torch.bfloat16)
-        g = torch.nn.functional.logsigmoid(torch.randn(1, T, P, generator=gen) + 2.0)
-        g = g.view(1, chunks, 64, P).cumsum(2).view(1, T, P)
-        h0 = 0.1 * torch.randn(1, P, c["K"], c["V"], generator=gen)
-        bits = lambda t: t.contiguous().view(torch.int16).numpy().view(np.uint16)  # noqa: E731
-        return bits(k), bits(w), bits(u), g.numpy(), h0.numpy()
-
-    def timed(chunks):
-        a = sample(chunks)
-        t0 = time.perf_counter()
-        o.fwd_h(*a, mode="reference", n_threads=threads)
-        return time.perf_counter() - t0
-
-    t1 = timed(1)
+    t1 = cpu_time(cpu_sample(c, P, 1), threads)
     chunks = int(max(1, min(NT, budget_s / max(t1, 1e-4))))
-    dt = timed(chunks)
+    dt = cpu_time(cpu_sample(c, P, chunks), threads)
     pair_chunks_per_s = P * chunks / dt
     job_pair_chunks = c["B"] * c["H"] * NT
     tokens = c["B"] * c["T"]
@@ -409,18 +411,70 @@ def strong_scaling_leg(args, world, rank, dev, stream):
     }
 
 
+def copy_only_ms(host_in, host_out, dev, steps, world):
+    """The e2e leg's host<->device traffic alone: every input copied in on one
+    stream while every output is copied out on another, no kernel; CUDA events,
+    mean per step, max over ranks.  Its ratio to the e2e time says whether the
+    copies bound the end-to-end number."""
+    import torch
+    cur = torch.cuda.current_stream(dev)
+    dev_in = [torch.empty(x.shape, dtype=x.dtype, device=dev) for x in host_in]
+    dev_out = [torch.empty(x.shape, dtype=x.dtype, device=dev) for x in host_out]
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+
+    def once():
+        s_in.wait_stream(cur)
+        s_out.wait_stream(cur)
+        with torch.cuda.stream(s_in):
+            for d, h in zip(dev_in, host_in):
+                d.copy_(h, non_blocking=True)
+        with torch.cuda.stream(s_out):
+            for h, d in zip(host_out, dev_out):
+                h.copy_(d, non_blocking=True)
+        cur.wait_stream(s_in)
+        cur.wait_stream(s_out)
+
+    once()
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(cur)
+    for _ in range(steps):
+        once()
+    e1.record(cur)
+    torch.cuda.synchronize()
+    return max_over_ranks(e0.elapsed_time(e1) / steps, world)
+
+
 def run_reference_arm(args, cfg_name, c, world, rank):
+    """The reference arm: the CPU implementation of the path on this host's cores.
+    Each step runs the whole job (every (sequence, head) pair, every chunk) when
+    that fits about 3 s, so ms_per_step is the measured time of a step; a larger
+    job runs a fixed subset of pairs per step and says so."""
     if rank != 0:
         return 0
     K, W = args.steps, args.warmup
-    budget = max(0.05, min(3.0, 150.0 / max(1, K + W)))
-    rates = []
-    desc, threads = "", 0
+    threads = len(os.sched_getaffinity(0))
+    NT = (c["T"] + 63) // 64
+    pairs = c["B"] * c["H"]
+    probe = cpu_time(cpu_sample(c, min(threads, pairs), 1), threads)
+    est_pair_chunk_s = probe / min(threads, pairs) * threads  # wall time of `threads` pair-chunks in parallel
+    per_step = max(0.5, min(3.0, 150.0 / max(1, K + W)))
+    P = pairs
+    while P > threads and est_pair_chunk_s * (P / threads) * NT > per_step:
+        P = max(threads, P // 2)
+    sample = cpu_sample(c, P, NT)
+    times = []
     for i in range(W + K):
-        r, desc, threads = cpu_reference_rate(c, budget, 0)
+        dt = cpu_time(sample, threads)
         if i >= W:
-            rates.append(r)
-    value = statistics.median(rates)
+            times.append(dt)
+    step_s = statistics.median(times)
+    frac = P / pairs
+    value = c["B"] * c["T"] * frac / step_s
+    desc = (f"{P} of {pairs} (sequence, head) pairs x all {NT} chunks per step"
+            + ("" if P == pairs else f" ({frac:.3f} of the job; tokens/s counts that fraction of B*T)")
+            + f", median of {K} steps after {W} warm-up steps, {threads} threads")
     line = {
         "impl": "reference",
         "metric": "fwd_h tokens/s",
@@ -429,7 +483,8 @@ def run_reference_arm(args, cfg_name, c, world, rank):
         "n_gpus": args.gpus,
         "steps": K,
         "warmup": W,
-        "ms_per_step": 1000.0 * c["B"] * c["T"] / value,
+        "ms_per_step": 1000.0 * step_s,
+        "full_job_ms": 1000.0 * step_s / frac,
         "higher_is_better": True,
         "scaling": c["scaling"],
         "vs_baseline": None,
@@ -593,6 +648,10 @@ def main() -> int:
         torch.cuda.synchronize()
         e2e_ms = max_over_ranks(e0.elapsed_time(e1), world) / args.e2e_steps
         e2e_value = tokens_per_step / (e2e_ms / 1000.0)
+    copy_ms = None
+    if args.e2e_steps > 0:
+        host_in = [x for n, x in host.items() if x is not None and n not in ("cu_seqlens", "chunk_indices")]
+        copy_ms = copy_only_ms(host_in, host_out, dev, args.e2e_steps, world)
 
     nbytes = config_bytes(c, 1000 + rank, has_h0=inp["initial_state"] is not None)
     if "chunk_indices" in inp:
@@ -649,7 +708,9 @@ def main() -> int:
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": e2e_ms,
                     "copy_gbs_per_rank": None if e2e_ms is None else (h2d + d2h) / (e2e_ms / 1000.0) / 1e9,
-                    "copy_gbs_total": None if e2e_ms is None else world * (h2d + d2h) / (e2e_ms / 1000.0) / 1e9},
+                    "copy_gbs_total": None if e2e_ms is None else world * (h2d + d2h) / (e2e_ms / 1000.0) / 1e9,
+                    "copy_only_ms_per_step": copy_ms,
+                    "e2e_over_copy_only": None if copy_ms is None else e2e_ms / copy_ms},
             "cpu_baseline": cpu,
             "parity": parity,
             "strong_scaling": strong,
