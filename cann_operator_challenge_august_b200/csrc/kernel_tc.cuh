@@ -73,7 +73,7 @@ struct TcConfig {
     static constexpr int kOffVout = kOffS + kSBytes;
     static constexpr int kOffG = kOffVout + kVoutBytes;  // [STAGES][64] fp32 gate inputs
     static constexpr int kOffBar = kOffG + STAGES * 64 * 4;
-    static constexpr int kNumBars = 2 * STAGES + 5;
+    static constexpr int kNumBars = 2 * STAGES + 11;  // + mma1/2_done, drain, s_ready[4], vdec_ready[4]
     static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;  // + tmem slot, abort flag, alignment
     static constexpr uint32_t kStageTx = kStageBytes;
     // MMA2 (M = K) as M = 128 halves when K = 256: D2 rows [128 m, 128 m + 128) at TMEM
@@ -170,9 +170,11 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
     uint64_t* empty = bars + STAGES;
     uint64_t* mma1_done = bars + 2 * STAGES;
     uint64_t* mma2_done = mma1_done + 1;
-    uint64_t* vdec_ready = mma1_done + 2;
+    uint64_t* mma_drain = mma1_done + 2;
+    // per TMEM lane quadrant: its warps wrote their rows of S (MMA1 may take those k
+    // steps) / their token rows of v_decay (MMA2 may take that k step)
     uint64_t* s_ready = mma1_done + 3;
-    uint64_t* mma_drain = mma1_done + 4;
+    uint64_t* vdec_ready = mma1_done + 7;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Cfg::kNumBars);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     volatile int* never_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);  // drains ignore aborts
@@ -203,8 +205,10 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
         }
         mbar_init(mma1_done, 1);
         mbar_init(mma2_done, 1);
-        mbar_init(vdec_ready, Cfg::kEpiWarps);
-        mbar_init(s_ready, Cfg::kEpiWarps);
+        for (int q4 = 0; q4 < 4; ++q4) {
+            mbar_init(&s_ready[q4], EW);
+            mbar_init(&vdec_ready[q4], EW);
+        }
         mbar_init(mma_drain, 1);
         *abort_flag = 0;
         *never_flag = 0;
@@ -290,36 +294,66 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
         for (int64_t c = 0; c < nchunks; ++c) {
             const int s = static_cast<int>(c % STAGES);
             if (!wait_warp(&full[s], static_cast<uint32_t>(c / STAGES) & 1)) break;
-            if (!wait_warp(s_ready, static_cast<uint32_t>(c) & 1)) break;
-            tc_fence_after();
             // descriptors differ only in the start-address field (bits 0-13, 16-byte units)
             const uint64_t a1 = umma_desc_sw128(wc_addr(s), 16, 1024);
             const uint64_t b1 = umma_desc_mn<Cfg::kSw64>(s_addr, Cfg::kSSubBytes);
-            if (elect_one_sync()) {
+            auto mma1_step = [&](int kk) {
+                tc_mma_bf16(d1, a1 + static_cast<uint64_t>(((kk >> 2) * 8192 + (kk & 3) * 32) >> 4),
+                            b1 + static_cast<uint64_t>((kk * 16 * Cfg::kRowB) >> 4), Cfg::kIdesc1, kk > 0 ? 1u : 0u);
+            };
+            // MMA1 k step kk reads S rows 16 kk..16 kk+15, which the warps of lane quadrant
+            // kk / (K / 64) write (K = 64: one step per quadrant; K = 128: two; K = 256: two
+            // per half, the second half's rows being done with the first's).  Issue each
+            // quadrant's steps as soon as its rows are in, in the fixed k order.
+            bool go = true;
 #pragma unroll
-                for (int kk = 0; kk < K_ / 16; ++kk)
-                    tc_mma_bf16(d1, a1 + static_cast<uint64_t>(((kk >> 2) * 8192 + (kk & 3) * 32) >> 4),
-                                b1 + static_cast<uint64_t>((kk * 16 * Cfg::kRowB) >> 4), Cfg::kIdesc1, kk > 0 ? 1u : 0u);
-                tc_commit(mma1_done);
+            for (int q4 = 0; q4 < 4; ++q4) {
+                if (!wait_warp(&s_ready[q4], static_cast<uint32_t>(c) & 1)) {
+                    go = false;
+                    break;
+                }
+                tc_fence_after();
+                if (elect_one_sync()) {
+                    constexpr int kPerQ = K_ == 64 ? 1 : 2;
+#pragma unroll
+                    for (int j = 0; j < kPerQ; ++j) mma1_step(q4 * kPerQ + j);
+                    if (q4 == 3) {
+                        if constexpr (K_ == 256) {
+#pragma unroll
+                            for (int kk = 8; kk < 16; ++kk) mma1_step(kk);
+                        }
+                        tc_commit(mma1_done);
+                    }
+                }
+                __syncwarp();
             }
-            __syncwarp();
-            if (!wait_warp(vdec_ready, static_cast<uint32_t>(c) & 1)) break;
-            tc_fence_after();
+            if (!go) break;
             const uint64_t a2 = umma_desc_sw128(kc_addr(s), 8192, 1024);
             const uint64_t b2 = umma_desc_mn<Cfg::kSw64>(uc_addr(s), Cfg::kUSub);
-            if (elect_one_sync()) {
-                // M = K halves (K = 256): rows 128 m.. of k_c start 2 m sub-tiles in
+            // MMA2 k step tt reads token rows 16 tt..16 tt+15 of v_decay, which the warps of
+            // quadrant tt write.  With M = K halves (K = 256: rows 128 m.. of k_c start 2 m
+            // sub-tiles in) each half accumulates its steps in the same order as before.
 #pragma unroll
-                for (int m = 0; m < Cfg::kM2Halves; ++m)
+            for (int tt = 0; tt < 4; ++tt) {
+                if (!wait_warp(&vdec_ready[tt], static_cast<uint32_t>(c) & 1)) {
+                    go = false;
+                    break;
+                }
+                tc_fence_after();
+                if (elect_one_sync()) {
 #pragma unroll
-                    for (int tt = 0; tt < 4; ++tt)
+                    for (int m = 0; m < Cfg::kM2Halves; ++m)
                         tc_mma_bf16(d2 + m * VT, a2 + static_cast<uint64_t>((m * 2 * 8192 + tt * 2048) >> 4),
                                     b2 + static_cast<uint64_t>((tt * 16 * Cfg::kRowB) >> 4), Cfg::kIdesc2,
                                     tt > 0 ? 1u : 0u);
-                tc_commit(mma2_done);
-                tc_commit(&empty[s]);
+                    if (tt == 3) {
+                        tc_commit(mma2_done);
+                        tc_commit(&empty[s]);
+                    }
+                }
+                __syncwarp();
             }
-            __syncwarp();
+            if (!go) break;
         }
         // Drain: every MMA this warp issued has completed before the TMEM it writes
         // is released (matters only on an abort path).
@@ -472,7 +506,7 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
         tc_fence_before();
         __syncwarp();
         if (nchunks > 0) store_h(0);
-        if (lane == 0) mbar_arrive(s_ready);
+        if (lane == 0) mbar_arrive(&s_ready[q]);
 
         for (int64_t c = 0; c < nchunks && ok; ++c) {
             const int s = static_cast<int>(c % STAGES);
@@ -588,7 +622,7 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
             fence_proxy_async_smem();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(vdec_ready);
+            if (lane == 0) mbar_arrive(&vdec_ready[q]);
             // v_new while MMA2 runs.
             const bool v_stored = p.v_new && !partial_varlen;
             if (kDeferVnew && p.v_new) {
@@ -728,7 +762,7 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
                 fence_proxy_async_smem();
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(s_ready);  // MMA1 and the h store both only read the tile
+                if (lane == 0) mbar_arrive(&s_ready[q]);  // MMA1 and the h store both only read the tile
                 store_h(c + 1);
             } else {
                 tc_fence_before();
