@@ -220,6 +220,20 @@ __device__ __forceinline__ void ref_state_x2(float& s0, float& s1, float a0, flo
     s1 = __high2float(sum);
 }
 
+// Epilogue 2 of the reference chain on a pair whose update is already in f16 (bits
+// `up`, finite), for a finite state and 0 <= alpha <= 1: the decayed state
+// fp16(fp16(S) * alpha) then stays within the f16 range, so it needs no saturation.
+__device__ __forceinline__ void ref_state_x2_fast(float& s0, float& s1, uint32_t up, __half2 alpha)
+{
+    const __half2 sh = bits_h2(f16x2_satfinite(s0, s1));
+    const __half2 hd = __hmul2_rn(sh, alpha);
+    const uint32_t hb = bf16x2_of_h2(hd), ub = bf16x2_of_h2(bits_h2(up));
+    const __nv_bfloat162 sum =
+        __hadd2_rn(*reinterpret_cast<const __nv_bfloat162*>(&hb), *reinterpret_cast<const __nv_bfloat162*>(&ub));
+    s0 = __low2float(sum);
+    s1 = __high2float(sum);
+}
+
 // max that propagates NaN (so a NaN operand fails a later `< bound` test)
 __device__ __forceinline__ float fmax_nan(float a, float b)
 {

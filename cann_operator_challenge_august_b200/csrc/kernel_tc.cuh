@@ -452,6 +452,16 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
                 st[i] = ref ? round_bf16(x) : x;
             }
         }
+        // Reference arithmetic: whether every state value of the warp is finite (the
+        // packed epilogue-2 chain needs it); a chunk on the packed chain keeps it so.
+        auto state_all_finite = [&]() {
+            float m = 0.0f;
+#pragma unroll
+            for (int i = 0; i < kNState; ++i) m = fmax_nan(m, fabsf(st[i]));
+            return __all_sync(0xffffffffu, m < INFINITY) != 0;
+        };
+        bool state_ok = REF ? state_all_finite() : true;
+        bool state_recheck = false;
         auto write_state_tile = [&]() {
             if constexpr (K_ >= 128) {
                 const int row = e2_row;
@@ -558,20 +568,24 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
                 tmem_ld_16x256b_x4(tmem + ((32u * q) << 16) + static_cast<uint32_t>(cbase + 32 * cb), acc[cb]);
             tmem_wait_ld();
             // v_decay only (the MMA2 operand); v_new is packed after MMA2 is released.
+            // Reference arithmetic: when every |u| and every |GEMM output| of the warp lies
+            // below 16384 (so u - ws stays in the f16 range) and both gates lie in [0, 1]
+            // (so v_new * gate cannot grow), the packed f16x2 chain needs no saturation and
+            // gives the scalar chain's bits; any other value in the warp (NaN, inf, out of
+            // range) sends the warp through the scalar chain.
             bool packed_ref = false;
-            if (ref) {
-                // The packed f16x2 chain is exact for finite operands below the f16 range;
-                // any other value in the warp sends the warp through the scalar chain.
-                float m = max_abs2(gate_a, gate_b);
+            if constexpr (REF) {
+                float m = 0.0f;
 #pragma unroll
                 for (int i = 0; i < kPairs; ++i) {
                     const int cb = i >> 3, j = (i >> 1) & 3, half = i & 1;
                     const float2 uu = unpack_bf16x2(uraw[i]);
-                    m = fmax_nan(m, fmax_nan(max_abs2(uu.x, uu.y),
-                                             max_abs2(__uint_as_float(acc[cb][4 * j + 2 * half]),
-                                                      __uint_as_float(acc[cb][4 * j + 2 * half + 1]))));
+                    m = fmax_nan(m, fabsf(uu.x));
+                    m = fmax_nan(m, fabsf(uu.y));
+                    m = fmax_nan(m, fabsf(__uint_as_float(acc[cb][4 * j + 2 * half])));
+                    m = fmax_nan(m, fabsf(__uint_as_float(acc[cb][4 * j + 2 * half + 1])));
                 }
-                packed_ref = __all_sync(0xffffffffu, m < 65000.0f) != 0;
+                packed_ref = __all_sync(0xffffffffu, m < 16384.0f && gate_a <= 1.0f && gate_b <= 1.0f) != 0;
             }
             if (packed_ref) {
                 const __half2 ga = __float2half2_rn(gate_a), gb = __float2half2_rn(gate_b);
@@ -579,12 +593,13 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
                 for (int i = 0; i < kPairs; ++i) {
                     const int cb = i >> 3, j = (i >> 1) & 3, half = i & 1;
                     const float2 uu = unpack_bf16x2(uraw[i]);
-                    uint32_t vd;
-                    ref_vnew_vdecay_x2(uu.x, uu.y, __uint_as_float(acc[cb][4 * j + 2 * half]),
-                                       __uint_as_float(acc[cb][4 * j + 2 * half + 1]), half ? gb : ga, vns[i], vd);
-                    vds[i] = (half ? tb : ta) < len ? vd : 0u;
+                    const __half2 ws = ref_gemm_to_f16x2(__uint_as_float(acc[cb][4 * j + 2 * half]),
+                                                         __uint_as_float(acc[cb][4 * j + 2 * half + 1]));
+                    const __half2 vn = __hsub2_rn(__floats2half2_rn(uu.x, uu.y), ws);
+                    vns[i] = h2_bits(vn);
+                    vds[i] = (half ? tb : ta) < len ? bf16x2_of_h2(__hmul2_rn(vn, half ? gb : ga)) : 0u;
                     if constexpr (!kDeferVnew) {
-                        const float2 f = __half22float2(bits_h2(vns[i]));
+                        const float2 f = __half22float2(vn);
                         vos[i] = (half ? tb : ta) < len ? pack_bf16x2(f.x, f.y) : 0u;
                     }
                 }
@@ -713,16 +728,17 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
                     tmem_ld_32x32b_x16(ta2 + 32 * cb + 16, r[1]);
                     if (cb == 0) wait_s_free();
                     tmem_wait_ld();
+                    // Reference arithmetic: the packed chain without saturation applies to a
+                    // finite state (tracked across chunks), 0 <= alpha <= 1 and GEMM outputs
+                    // below 32768 in magnitude (finite in f16), else the scalar chain.
                     bool packed_ref = false;
-                    if (ref) {
-                        float m = fabsf(alpha);
+                    if constexpr (REF) {
+                        float m = 0.0f;
 #pragma unroll
                         for (int j = 0; j < 2; ++j)
 #pragma unroll
-                            for (int i = 0; i < 16; i += 2)
-                                m = fmax_nan(m, fmax_nan(max_abs2(st[32 * cb + 16 * j + i], st[32 * cb + 16 * j + i + 1]),
-                                                         max_abs2(__uint_as_float(r[j][i]), __uint_as_float(r[j][i + 1]))));
-                        packed_ref = __all_sync(0xffffffffu, m < INFINITY) != 0;
+                            for (int i = 0; i < 16; ++i) m = fmax_nan(m, fabsf(__uint_as_float(r[j][i])));
+                        packed_ref = __all_sync(0xffffffffu, state_ok && alpha <= 1.0f && m < 32768.0f) != 0;
                     }
                     if (packed_ref) {
                         const __half2 ah = __float2half2_rn(alpha);
@@ -730,9 +746,12 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
                         for (int j = 0; j < 2; ++j)
 #pragma unroll
                             for (int i = 0; i < 16; i += 2)
-                                ref_state_x2(st[32 * cb + 16 * j + i], st[32 * cb + 16 * j + i + 1],
-                                             __uint_as_float(r[j][i]), __uint_as_float(r[j][i + 1]), ah);
+                                ref_state_x2_fast(st[32 * cb + 16 * j + i], st[32 * cb + 16 * j + i + 1],
+                                                  h2_bits(ref_gemm_to_f16x2(__uint_as_float(r[j][i]),
+                                                                            __uint_as_float(r[j][i + 1]))),
+                                                  ah);
                     } else {
+                        if constexpr (REF) state_recheck = true;
 #pragma unroll
                         for (int j = 0; j < 2; ++j)
 #pragma unroll
@@ -741,6 +760,12 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
                                 sv = ref ? ref_state(sv, alpha, __uint_as_float(r[j][i]))
                                          : fmaf(sv, alpha, __uint_as_float(r[j][i]));
                             }
+                    }
+                }
+                if constexpr (REF) {
+                    if (state_recheck) {  // warp-uniform: set on the scalar chain only
+                        state_ok = state_all_finite();
+                        state_recheck = false;
                     }
                 }
             } else {
