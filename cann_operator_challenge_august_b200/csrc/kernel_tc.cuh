@@ -157,6 +157,40 @@ __device__ __forceinline__ float2 unpack_bf16x2(uint32_t v)
     return make_float2(__uint_as_float(v << 16), __uint_as_float(v & 0xffff0000u));
 }
 
+// The epilogue's state values: fp32 for the fp32-state arithmetic or, for the
+// reference arithmetic, whose state is bf16 between chunks, bf16 pairs packed two to
+// a register (values i, i + 1 with i even share a register: same row, adjacent columns).
+template <bool PACKED, int N>
+struct StateRegs {
+    float f[PACKED ? 1 : N];
+    uint32_t b[PACKED ? N / 2 : 1];
+    __device__ __forceinline__ float get(int i) const
+    {
+        if constexpr (PACKED)
+            return __uint_as_float((i & 1) ? (b[i >> 1] & 0xffff0000u) : (b[i >> 1] << 16));
+        else
+            return f[i];
+    }
+    // bf16 bits of values i, i + 1 (i even)
+    __device__ __forceinline__ uint32_t pair_bits(int i) const
+    {
+        if constexpr (PACKED)
+            return b[i >> 1];
+        else
+            return pack_bf16x2(f[i], f[i + 1]);
+    }
+    // values i, i + 1 (i even); rounded to bf16 when packed
+    __device__ __forceinline__ void set_pair(int i, float lo, float hi)
+    {
+        if constexpr (PACKED) {
+            b[i >> 1] = pack_bf16x2(lo, hi);
+        } else {
+            f[i] = lo;
+            f[i + 1] = hi;
+        }
+    }
+};
+
 template <int K_, int VT, int STAGES, int EW, bool REF>
 __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConfig<K_, VT, STAGES, EW>::kMinBlocks)
     fwd_h_tc_kernel(const __grid_constant__ TcArgs args)
@@ -385,7 +419,7 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
         const int e2_c0 = (K_ == 256) ? 0 : cbase;
         const int kdim = static_cast<int>(p.K);
         const int64_t vdim = p.V;
-        float st[kNState];
+        StateRegs<REF, kNState> st;
         auto st_row_col = [&](int i, int& row, int& col) {
             if constexpr (K_ >= 128) {
                 row = e2_row;
@@ -418,38 +452,45 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
                 if (reinterpret_cast<uintptr_t>(h0_run) & 15) h0_run = nullptr;
             }
         }
-        if (h0_run) {
-            if (p.h0_dtype == kBF16) {
+        bool h0_loaded = false;
+        if constexpr (kVecState) {
+            if (h0_run) {
+                h0_loaded = true;
+                if (p.h0_dtype == kBF16) {
 #pragma unroll
-                for (int j = 0; j < kNState / 8; ++j) {
-                    const uint4 x = reinterpret_cast<const uint4*>(h0_run)[j];
-                    const uint32_t w4[4] = {x.x, x.y, x.z, x.w};
+                    for (int j = 0; j < kNState / 8; ++j) {
+                        const uint4 x = reinterpret_cast<const uint4*>(h0_run)[j];
+                        const uint32_t w4[4] = {x.x, x.y, x.z, x.w};
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const float2 f = unpack_bf16x2(w4[e]);
-                        st[8 * j + 2 * e] = f.x;
-                        st[8 * j + 2 * e + 1] = f.y;
+                        for (int e = 0; e < 4; ++e) {
+                            const float2 f = unpack_bf16x2(w4[e]);
+                            st.set_pair(8 * j + 2 * e, f.x, f.y);
+                        }
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < kNState / 4; ++j) {
+                        const float4 x = reinterpret_cast<const float4*>(h0_run)[j];
+                        st.set_pair(4 * j, x.x, x.y);
+                        st.set_pair(4 * j + 2, x.z, x.w);
                     }
                 }
-            } else {
-#pragma unroll
-                for (int j = 0; j < kNState / 4; ++j) {
-                    const float4 x = reinterpret_cast<const float4*>(h0_run)[j];
-                    st[4 * j] = ref ? round_bf16(x.x) : x.x;
-                    st[4 * j + 1] = ref ? round_bf16(x.y) : x.y;
-                    st[4 * j + 2] = ref ? round_bf16(x.z) : x.z;
-                    st[4 * j + 3] = ref ? round_bf16(x.w) : x.w;
-                }
             }
-        } else {
+        }
+        if (!h0_loaded) {
+            // pairs of adjacent columns of one row; the reference arithmetic rounds the
+            // initial state to bf16 (packing does)
 #pragma unroll
-            for (int i = 0; i < kNState; ++i) {
+            for (int i = 0; i < kNState; i += 2) {
                 int row, col;
                 st_row_col(i, row, col);
-                float x = 0.0f;
-                if (p.h0 && row < kdim && v0 + col < vdim)
-                    x = load_io(p.h0, p.h0_dtype, si.n * p.h0_sn + hv * p.h0_sh + row * p.h0_sk + (v0 + col) * p.h0_sv);
-                st[i] = ref ? round_bf16(x) : x;
+                float x0 = 0.0f, x1 = 0.0f;
+                if (p.h0 && row < kdim) {
+                    const int64_t at = si.n * p.h0_sn + hv * p.h0_sh + row * p.h0_sk;
+                    if (v0 + col < vdim) x0 = load_io(p.h0, p.h0_dtype, at + (v0 + col) * p.h0_sv);
+                    if (v0 + col + 1 < vdim) x1 = load_io(p.h0, p.h0_dtype, at + (v0 + col + 1) * p.h0_sv);
+                }
+                st.set_pair(i, x0, x1);
             }
         }
         // Reference arithmetic: whether every state value of the warp is finite (the
@@ -457,7 +498,7 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
         auto state_all_finite = [&]() {
             float m = 0.0f;
 #pragma unroll
-            for (int i = 0; i < kNState; ++i) m = fmax_nan(m, fabsf(st[i]));
+            for (int i = 0; i < kNState; ++i) m = fmax_nan(m, fabsf(st.get(i)));
             return __all_sync(0xffffffffu, m < INFINITY) != 0;
         };
         bool state_ok = REF ? state_all_finite() : true;
@@ -468,10 +509,10 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
 #pragma unroll
                 for (int j = 0; j < Cfg::kE2Cols / 8; ++j) {
                     uint4 v;
-                    v.x = pack_bf16x2(st[8 * j + 0], st[8 * j + 1]);
-                    v.y = pack_bf16x2(st[8 * j + 2], st[8 * j + 3]);
-                    v.z = pack_bf16x2(st[8 * j + 4], st[8 * j + 5]);
-                    v.w = pack_bf16x2(st[8 * j + 6], st[8 * j + 7]);
+                    v.x = st.pair_bits(8 * j + 0);
+                    v.y = st.pair_bits(8 * j + 2);
+                    v.z = st.pair_bits(8 * j + 4);
+                    v.w = st.pair_bits(8 * j + 6);
                     *reinterpret_cast<uint4*>(s_tile + tile_off<Cfg::kSw64>(row, e2_c0 + 8 * j, Cfg::kSSubBytes)) = v;
                 }
             } else {
@@ -479,8 +520,7 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
                 for (int i = 0; i < kNState; i += 2) {
                     int row, col;
                     st_row_col(i, row, col);
-                    *reinterpret_cast<uint32_t*>(s_tile + sw128_off(row, col, Cfg::kSSubBytes)) =
-                        pack_bf16x2(st[i], st[i + 1]);
+                    *reinterpret_cast<uint32_t*>(s_tile + sw128_off(row, col, Cfg::kSSubBytes)) = st.pair_bits(i);
                 }
             }
         };
@@ -745,20 +785,27 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
 #pragma unroll
                         for (int j = 0; j < 2; ++j)
 #pragma unroll
-                            for (int i = 0; i < 16; i += 2)
-                                ref_state_x2_fast(st[32 * cb + 16 * j + i], st[32 * cb + 16 * j + i + 1],
-                                                  h2_bits(ref_gemm_to_f16x2(__uint_as_float(r[j][i]),
-                                                                            __uint_as_float(r[j][i + 1]))),
+                            for (int i = 0; i < 16; i += 2) {
+                                const int si2 = 32 * cb + 16 * j + i;
+                                float s0 = st.get(si2), s1 = st.get(si2 + 1);
+                                ref_state_x2_fast(s0, s1, h2_bits(ref_gemm_to_f16x2(__uint_as_float(r[j][i]),
+                                                                                    __uint_as_float(r[j][i + 1]))),
                                                   ah);
+                                st.set_pair(si2, s0, s1);
+                            }
                     } else {
                         if constexpr (REF) state_recheck = true;
 #pragma unroll
                         for (int j = 0; j < 2; ++j)
 #pragma unroll
-                            for (int i = 0; i < 16; ++i) {
-                                float& sv = st[32 * cb + 16 * j + i];
-                                sv = ref ? ref_state(sv, alpha, __uint_as_float(r[j][i]))
-                                         : fmaf(sv, alpha, __uint_as_float(r[j][i]));
+                            for (int i = 0; i < 16; i += 2) {
+                                const int si2 = 32 * cb + 16 * j + i;
+                                const float a0 = __uint_as_float(r[j][i]), a1 = __uint_as_float(r[j][i + 1]);
+                                const float s0 = st.get(si2), s1 = st.get(si2 + 1);
+                                if (ref)
+                                    st.set_pair(si2, ref_state(s0, alpha, a0), ref_state(s1, alpha, a1));
+                                else
+                                    st.set_pair(si2, fmaf(s0, alpha, a0), fmaf(s1, alpha, a1));
                             }
                     }
                 }
@@ -776,9 +823,13 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
                     tmem_ld_16x256b_x4(tmem + VT + ((32u * q) << 16) + static_cast<uint32_t>(cbase + 32 * cb), r);
                     tmem_wait_ld();
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        float& sv = st[16 * cb + i];
-                        sv = ref ? ref_state(sv, alpha, __uint_as_float(r[i])) : fmaf(sv, alpha, __uint_as_float(r[i]));
+                    for (int i = 0; i < 16; i += 2) {
+                        const float a0 = __uint_as_float(r[i]), a1 = __uint_as_float(r[i + 1]);
+                        const float s0 = st.get(16 * cb + i), s1 = st.get(16 * cb + i + 1);
+                        if (ref)
+                            st.set_pair(16 * cb + i, ref_state(s0, alpha, a0), ref_state(s1, alpha, a1));
+                        else
+                            st.set_pair(16 * cb + i, fmaf(s0, alpha, a0), fmaf(s1, alpha, a1));
                     }
                 }
             }
@@ -808,12 +859,13 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
 #pragma unroll
                 for (int j = 0; j < kNState / 8; ++j)
                     reinterpret_cast<uint4*>(f_run)[j] =
-                        make_uint4(pack_bf16x2(st[8 * j], st[8 * j + 1]), pack_bf16x2(st[8 * j + 2], st[8 * j + 3]),
-                                   pack_bf16x2(st[8 * j + 4], st[8 * j + 5]), pack_bf16x2(st[8 * j + 6], st[8 * j + 7]));
+                        make_uint4(st.pair_bits(8 * j), st.pair_bits(8 * j + 2), st.pair_bits(8 * j + 4),
+                                   st.pair_bits(8 * j + 6));
             } else if (f_run) {
 #pragma unroll
                 for (int j = 0; j < kNState / 4; ++j)
-                    reinterpret_cast<float4*>(f_run)[j] = make_float4(st[4 * j], st[4 * j + 1], st[4 * j + 2], st[4 * j + 3]);
+                    reinterpret_cast<float4*>(f_run)[j] =
+                        make_float4(st.get(4 * j), st.get(4 * j + 1), st.get(4 * j + 2), st.get(4 * j + 3));
             } else {
 #pragma unroll
                 for (int i = 0; i < kNState; ++i) {
@@ -821,7 +873,7 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
                     st_row_col(i, row, col);
                     if (row < kdim && v0 + col < vdim)
                         store_io(p.final_state, p.f_dtype,
-                                 si.n * p.f_sn + hv * p.f_sh + row * p.f_sk + (v0 + col) * p.f_sv, st[i]);
+                                 si.n * p.f_sn + hv * p.f_sh + row * p.f_sk + (v0 + col) * p.f_sv, st.get(i));
                 }
             }
         }
