@@ -53,6 +53,13 @@ struct Dims {
 
 int io_of(int32_t dt) { return dt == CGDR_DT_BF16 ? kBF16 : (dt == CGDR_DT_FLOAT32 ? kF32 : 0); }
 
+// Whether a tensor-core plan runs the sixteen-warp epilogue (K tile 128, 128-column tiles,
+// reference arithmetic): its v_new staging is per warp, 32 columns with the 64-byte swizzle.
+bool tc_quarters(const cgdrFwdHPlan& pl)
+{
+    return pl.kernel == 1 && pl.v_tile == 128 && pl.block == TcConfig<128, 128, 3, 4>::kThreads;
+}
+
 // K tile of the tensor-core kernel for head width K (0: no tensor-core kernel).
 int tc_k_tile(int64_t K)
 {
@@ -317,8 +324,13 @@ cgdrStatus build(const cgdrTensor* k, const cgdrTensor* w, const cgdrTensor* u, 
         pl.kernel = 1;
         pl.v_tile = vt;
         pl.stages = (vt == 64) ? 2 : 3;
-        pl.block = kt == 256 ? TcConfig<256, 64, 2, 2>::kThreads
-                   : vt == 128 ? TcConfig<128, 128, 3, 2>::kThreads : TcConfig<128, 64, 2, 1>::kThreads;
+        // The reference arithmetic's 128-column tiles (K tile 128) run sixteen epilogue
+        // warps (four 32-column quarters per lane quadrant): its epilogues issue about twice
+        // the instructions of the fp32-state ones.
+        pl.block = kt == 256                      ? TcConfig<256, 64, 2, 2>::kThreads
+                   : (vt == 128 && kt == 128 && ref) ? TcConfig<128, 128, 3, 4>::kThreads
+                   : vt == 128                    ? TcConfig<128, 128, 3, 2>::kThreads
+                                                  : TcConfig<128, 64, 2, 1>::kThreads;
     } else {
         if (d.K < 1 || d.K > kMaxHeadDim) {
             delete ex_;
@@ -340,7 +352,7 @@ cgdrStatus build(const cgdrTensor* k, const cgdrTensor* w, const cgdrTensor* u, 
         if (kt == 256)
             pl.smem_bytes = CGDR_SMEM(256, 64, 2, 2);
         else if (kt == 128)
-            pl.smem_bytes = pl.v_tile == 128  ? CGDR_SMEM(128, 128, 3, 2)
+            pl.smem_bytes = pl.v_tile == 128  ? (ref ? CGDR_SMEM(128, 128, 3, 4) : CGDR_SMEM(128, 128, 3, 2))
                             : pl.v_tile == 64 ? CGDR_SMEM(128, 64, 2, 1)
                                               : CGDR_SMEM(128, 32, 3, 1);
         else
@@ -385,7 +397,7 @@ cgdrStatus build_maps(const cgdrExecutor* ex, TcMaps* m)
     }
     if (p.v_new) {
         // the K tile 256 kernel stages v_new per warp in 32-column regions (64-byte swizzle)
-        const bool v32 = sw64 || tc_k_tile(p.K) == 256;
+        const bool v32 = sw64 || tc_k_tile(p.K) == 256 || tc_quarters(ex->plan);
         const int64_t size[4] = {p.V, p.H, p.T, p.B}, stride[4] = {1, p.v_sh, p.v_st, p.v_sb};
         const uint32_t box[4] = {v32 ? 32u : 64u, 1, 16, 1};
         if ((st = make_map(&m->v, p.v_new, 4, size, stride, box, "v", v32 ? 64 : 128))) return st;
@@ -529,6 +541,8 @@ cgdrStatus fwd_h_enqueue(const cgdrExecutor* executor, int* status, uint8_t* met
         const int kt = tc_k_tile(p.K);
         if (kt == 256)
             e = launch_tc_numerics<256, 64, 2, 2>(args, grid, stream);
+        else if (kt == 128 && tc_quarters(pl))
+            e = launch_tc<128, 128, 3, 4, true>(args, grid, stream);
         else if (kt == 128)
             e = pl.v_tile == 128  ? launch_tc_numerics<128, 128, 3, 2>(args, grid, stream)
                 : pl.v_tile == 64 ? launch_tc_numerics<128, 64, 2, 1>(args, grid, stream)

@@ -46,8 +46,9 @@ template <int K_, int VT, int STAGES, int EW>
 struct TcConfig {
     static_assert(K_ == 64 || K_ == 128 || K_ == 256, "tensor-core path: K tile in {64, 128, 256}");
     static_assert(VT == 32 || VT == 64 || VT == 128, "tensor-core path: V tile in {32, 64, 128}");
-    static_assert(EW == 1 || EW == VT / 64 || (K_ == 256 && VT == 64 && EW == 2),
-                  "column split must be 1, one warp per 64-column sub-tile, or (K = 256) two 32-column halves");
+    static_assert(EW == 1 || EW == VT / 64 || (K_ == 256 && VT == 64 && EW == 2) || (K_ == 128 && VT == 128 && EW == 4),
+                  "column split must be 1, one warp per 64-column sub-tile, (K = 256) two 32-column halves, or "
+                  "(K = 128, VT = 128) four 32-column quarters");
     static_assert(VT != 32 || K_ == 128, "32-column tiles: K = 128");
     static_assert(K_ != 256 || VT == 64, "K = 256: 64-column tiles");
     // 32-column tiles keep u_c, v_new and S in 64-byte rows (64-byte swizzle);
@@ -73,7 +74,7 @@ struct TcConfig {
     static constexpr int kOffVout = kOffS + kSBytes;
     static constexpr int kOffG = kOffVout + kVoutBytes;  // [STAGES][64] fp32 gate inputs
     static constexpr int kOffBar = kOffG + STAGES * 64 * 4;
-    static constexpr int kNumBars = 2 * STAGES + 11;  // + mma1/2_done, drain, s_ready[4], vdec_ready[4]
+    static constexpr int kNumBars = 2 * STAGES + 15;  // + mma1/2_done, drain, s_ready[4], vdec_ready[4], h_read[4]
     static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;  // + tmem slot, abort flag, alignment
     static constexpr uint32_t kStageTx = kStageBytes;
     // MMA2 (M = K) as M = 128 halves when K = 256: D2 rows [128 m, 128 m + 128) at TMEM
@@ -92,6 +93,11 @@ struct TcConfig {
     // stages its v_new rows in a region of its own, 32 columns of 64-byte rows with the
     // 64-byte swizzle, and stores it with a 32-column box, so no two warps share a store.
     static constexpr bool kSplitVout = kCW < kSubCols;
+    // Epilogue-2 column slices narrower than a 64-column sub-tile (K = 128 with four
+    // 32-column quarters): the quadrant's warps at even slices store h for their
+    // sub-tile once the quadrant's rows are all written (s_ready), and the odd slices
+    // rewrite their half of the state tile only after that store has read it (h_read).
+    static constexpr bool kSharedH = K_ >= 128 && kE2Cols < kSubCols;
     static constexpr int kVoutRegion = 64 * 64;  // bytes of one warp's region (64 rows x 64 B)
     static constexpr int kMinBlocks = (VT == 64 && K_ != 256) ? 2 : 1;  // CTAs resident per SM the tile is sized for
     static constexpr uint32_t kIdesc1 = umma_idesc_bf16(64, VT, false, true);
@@ -209,6 +215,7 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
     // steps) / their token rows of v_decay (MMA2 may take that k step)
     uint64_t* s_ready = mma1_done + 3;
     uint64_t* vdec_ready = mma1_done + 7;
+    uint64_t* h_read = mma1_done + 11;  // per quadrant (kSharedH): the h store read the state tile
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Cfg::kNumBars);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     volatile int* never_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);  // drains ignore aborts
@@ -242,6 +249,7 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
         for (int q4 = 0; q4 < 4; ++q4) {
             mbar_init(&s_ready[q4], EW);
             mbar_init(&vdec_ready[q4], EW);
+            mbar_init(&h_read[q4], EW / 2 > 0 ? EW / 2 : 1);
         }
         mbar_init(mma_drain, 1);
         *abort_flag = 0;
@@ -550,13 +558,30 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
         constexpr bool kDeferVnew = VT <= 64;
         const uint32_t vo_base = Cfg::kSplitVout ? static_cast<uint32_t>(e * Cfg::kVoutRegion) : 0u;
 
+        // kSharedH: the warps at even column slices issue the h stores of their sub-tile
+        const bool h_issuer = !Cfg::kSharedH || (e & 1) == 0;
+        // kSharedH, issuer: wait until the quadrant's warps all wrote S_x (phase x of
+        // s_ready[q]), then store h[x]; false when the wait gave up
+        auto store_h_shared = [&](int64_t x) {
+            bool go = true;
+            if (lane == 0) go = mbar_wait(&s_ready[q], static_cast<uint32_t>(x) & 1, ctl, 0x40);
+            go = __shfl_sync(0xffffffffu, go ? 1 : 0, 0) != 0;
+            if (go) store_h(x);
+            return go;
+        };
+
         bool ok = true;
         write_state_tile();
         fence_proxy_async_smem();
         tc_fence_before();
         __syncwarp();
-        if (nchunks > 0) store_h(0);
-        if (lane == 0) mbar_arrive(&s_ready[q]);
+        if constexpr (Cfg::kSharedH) {
+            if (lane == 0) mbar_arrive(&s_ready[q]);
+            if (nchunks > 0 && h_issuer) ok = store_h_shared(0);
+        } else {
+            if (nchunks > 0) store_h(0);
+            if (lane == 0) mbar_arrive(&s_ready[q]);
+        }
 
         for (int64_t c = 0; c < nchunks && ok; ++c) {
             const int s = static_cast<int>(c % STAGES);
@@ -709,8 +734,14 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
                     }
                 }
             } else if (v_stored) {
-                // staging free: the store of chunk c-1 is read (only h[c]'s may be pending)
-                if (lane == 0) bulk_wait_group_read1();
+                // staging free: the store of chunk c-1 is read (only h[c]'s may be pending;
+                // a warp that stores no h has nothing newer than that store)
+                if (lane == 0) {
+                    if (h_issuer)
+                        bulk_wait_group_read1();
+                    else
+                        bulk_wait_group_read0();
+                }
                 __syncwarp();
                 if constexpr (Cfg::kSplitVout) {
 #pragma unroll
@@ -750,15 +781,24 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
             const bool more = c + 1 < nchunks;
             // S tile free once h[c]'s store is read (chunk c's v_new store may be pending);
             // the wait overlaps the TMEM loads.
+            // kSharedH: the issuers then tell the quadrant's other warps (h_read[q], phase c);
+            // those wait for it instead.  False when that wait gave up.
             auto wait_s_free = [&]() {
+                bool go = true;
                 if (lane == 0 && more) {
-                    if (v_stored)
-                        bulk_wait_group_read1();
-                    else
-                        bulk_wait_group_read0();
+                    if (h_issuer) {
+                        if (v_stored)
+                            bulk_wait_group_read1();
+                        else
+                            bulk_wait_group_read0();
+                        if constexpr (Cfg::kSharedH) mbar_arrive(&h_read[q]);
+                    } else {
+                        go = mbar_wait(&h_read[q], static_cast<uint32_t>(c) & 1, ctl, 0x40);
+                    }
                 }
-                __syncwarp();
+                return __shfl_sync(0xffffffffu, go ? 1 : 0, 0) != 0;
             };
+            bool s_free = true;
             if constexpr (K_ >= 128) {
                 const uint32_t ta2 = tmem + VT * (1 + (K_ == 256 ? e : 0)) + ((32u * q) << 16) + static_cast<uint32_t>(e2_c0);
 #pragma unroll
@@ -766,7 +806,7 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
                     uint32_t r[2][16];
                     tmem_ld_32x32b_x16(ta2 + 32 * cb, r[0]);
                     tmem_ld_32x32b_x16(ta2 + 32 * cb + 16, r[1]);
-                    if (cb == 0) wait_s_free();
+                    if (cb == 0) s_free = wait_s_free();
                     tmem_wait_ld();
                     // Reference arithmetic: the packed chain without saturation applies to a
                     // finite state (tracked across chunks), 0 <= alpha <= 1 and GEMM outputs
@@ -816,7 +856,7 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
                     }
                 }
             } else {
-                wait_s_free();
+                s_free = wait_s_free();
 #pragma unroll
                 for (int cb = 0; cb < Cfg::kCW / 32; ++cb) {
                     uint32_t r[16];
@@ -833,13 +873,26 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
                     }
                 }
             }
+            if (!s_free) {
+                ok = false;
+                break;
+            }
             if (more) {
                 write_state_tile();
                 fence_proxy_async_smem();
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&s_ready[q]);  // MMA1 and the h store both only read the tile
-                store_h(c + 1);
+                // MMA1 and the h store both only read the tile
+                if constexpr (Cfg::kSharedH) {
+                    if (lane == 0) mbar_arrive(&s_ready[q]);
+                    if (h_issuer && !store_h_shared(c + 1)) {
+                        ok = false;
+                        break;
+                    }
+                } else {
+                    if (lane == 0) mbar_arrive(&s_ready[q]);
+                    store_h(c + 1);
+                }
             } else {
                 tc_fence_before();
             }
