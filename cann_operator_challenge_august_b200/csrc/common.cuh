@@ -220,6 +220,17 @@ __device__ __forceinline__ void ref_state_x2(float& s0, float& s1, float a0, flo
     s1 = __high2float(sum);
 }
 
+// Epilogue 1 of the reference chain on a pair without saturations: exact when
+// |u|, |acc| < 16384 (so u - ws stays in the f16 range) and 0 <= gate <= 1 (so
+// v_new * gate cannot grow); callers check both for the whole warp first.
+__device__ __forceinline__ void ref_vnew_vdecay_x2_fast(float u0, float u1, float a0, float a1, __half2 gate,
+                                                        uint32_t& vn_bits, uint32_t& vd_bits)
+{
+    const __half2 vn = __hsub2_rn(__floats2half2_rn(u0, u1), ref_gemm_to_f16x2(a0, a1));
+    vn_bits = h2_bits(vn);
+    vd_bits = bf16x2_of_h2(__hmul2_rn(vn, gate));
+}
+
 // Epilogue 2 of the reference chain on a pair whose update is already in f16 (bits
 // `up`, finite), for a finite state and 0 <= alpha <= 1: the decayed state
 // fp16(fp16(S) * alpha) then stays within the f16 range, so it needs no saturation.

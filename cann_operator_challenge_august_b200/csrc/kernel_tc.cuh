@@ -74,7 +74,7 @@ struct TcConfig {
     static constexpr int kOffVout = kOffS + kSBytes;
     static constexpr int kOffG = kOffVout + kVoutBytes;  // [STAGES][64] fp32 gate inputs
     static constexpr int kOffBar = kOffG + STAGES * 64 * 4;
-    static constexpr int kNumBars = 2 * STAGES + 15;  // + mma1/2_done, drain, s_ready[4], vdec_ready[4], h_read[4]
+    static constexpr int kNumBars = 2 * STAGES + 9;  // + mma1/2_done, drain, s_ready, vdec_ready, h_read[4]
     static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;  // + tmem slot, abort flag, alignment
     static constexpr uint32_t kStageTx = kStageBytes;
     // MMA2 (M = K) as M = 128 halves when K = 256: D2 rows [128 m, 128 m + 128) at TMEM
@@ -95,7 +95,7 @@ struct TcConfig {
     static constexpr bool kSplitVout = kCW < kSubCols;
     // Epilogue-2 column slices narrower than a 64-column sub-tile (K = 128 with four
     // 32-column quarters): the quadrant's warps at even slices store h for their
-    // sub-tile once the quadrant's rows are all written (s_ready), and the odd slices
+    // sub-tile once every epilogue warp wrote its part (s_ready), and the odd slices
     // rewrite their half of the state tile only after that store has read it (h_read).
     static constexpr bool kSharedH = K_ >= 128 && kE2Cols < kSubCols;
     static constexpr int kVoutRegion = 64 * 64;  // bytes of one warp's region (64 rows x 64 B)
@@ -211,11 +211,9 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
     uint64_t* mma1_done = bars + 2 * STAGES;
     uint64_t* mma2_done = mma1_done + 1;
     uint64_t* mma_drain = mma1_done + 2;
-    // per TMEM lane quadrant: its warps wrote their rows of S (MMA1 may take those k
-    // steps) / their token rows of v_decay (MMA2 may take that k step)
-    uint64_t* s_ready = mma1_done + 3;
-    uint64_t* vdec_ready = mma1_done + 7;
-    uint64_t* h_read = mma1_done + 11;  // per quadrant (kSharedH): the h store read the state tile
+    uint64_t* s_ready = mma1_done + 3;     // every epilogue warp wrote its part of S
+    uint64_t* vdec_ready = mma1_done + 4;  // every epilogue warp wrote its rows of v_decay
+    uint64_t* h_read = mma1_done + 5;      // per quadrant (kSharedH): the h store read the state tile
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Cfg::kNumBars);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     volatile int* never_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);  // drains ignore aborts
@@ -246,11 +244,9 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
         }
         mbar_init(mma1_done, 1);
         mbar_init(mma2_done, 1);
-        for (int q4 = 0; q4 < 4; ++q4) {
-            mbar_init(&s_ready[q4], EW);
-            mbar_init(&vdec_ready[q4], EW);
-            mbar_init(&h_read[q4], EW / 2 > 0 ? EW / 2 : 1);
-        }
+        mbar_init(s_ready, Cfg::kEpiWarps);
+        mbar_init(vdec_ready, Cfg::kEpiWarps);
+        for (int q4 = 0; q4 < 4; ++q4) mbar_init(&h_read[q4], EW / 2 > 0 ? EW / 2 : 1);
         mbar_init(mma_drain, 1);
         *abort_flag = 0;
         *never_flag = 0;
@@ -339,63 +335,33 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
             // descriptors differ only in the start-address field (bits 0-13, 16-byte units)
             const uint64_t a1 = umma_desc_sw128(wc_addr(s), 16, 1024);
             const uint64_t b1 = umma_desc_mn<Cfg::kSw64>(s_addr, Cfg::kSSubBytes);
-            auto mma1_step = [&](int kk) {
-                tc_mma_bf16(d1, a1 + static_cast<uint64_t>(((kk >> 2) * 8192 + (kk & 3) * 32) >> 4),
-                            b1 + static_cast<uint64_t>((kk * 16 * Cfg::kRowB) >> 4), Cfg::kIdesc1, kk > 0 ? 1u : 0u);
-            };
-            // MMA1 k step kk reads S rows 16 kk..16 kk+15, which the warps of lane quadrant
-            // kk / (K / 64) write (K = 64: one step per quadrant; K = 128: two; K = 256: two
-            // per half, the second half's rows being done with the first's).  Issue each
-            // quadrant's steps as soon as its rows are in, in the fixed k order.
-            bool go = true;
+            if (!wait_warp(s_ready, static_cast<uint32_t>(c) & 1)) break;
+            tc_fence_after();
+            if (elect_one_sync()) {
 #pragma unroll
-            for (int q4 = 0; q4 < 4; ++q4) {
-                if (!wait_warp(&s_ready[q4], static_cast<uint32_t>(c) & 1)) {
-                    go = false;
-                    break;
-                }
-                tc_fence_after();
-                if (elect_one_sync()) {
-                    constexpr int kPerQ = K_ == 64 ? 1 : 2;
-#pragma unroll
-                    for (int j = 0; j < kPerQ; ++j) mma1_step(q4 * kPerQ + j);
-                    if (q4 == 3) {
-                        if constexpr (K_ == 256) {
-#pragma unroll
-                            for (int kk = 8; kk < 16; ++kk) mma1_step(kk);
-                        }
-                        tc_commit(mma1_done);
-                    }
-                }
-                __syncwarp();
+                for (int kk = 0; kk < K_ / 16; ++kk)
+                    tc_mma_bf16(d1, a1 + static_cast<uint64_t>(((kk >> 2) * 8192 + (kk & 3) * 32) >> 4),
+                                b1 + static_cast<uint64_t>((kk * 16 * Cfg::kRowB) >> 4), Cfg::kIdesc1, kk > 0 ? 1u : 0u);
+                tc_commit(mma1_done);
             }
-            if (!go) break;
+            __syncwarp();
+            if (!wait_warp(vdec_ready, static_cast<uint32_t>(c) & 1)) break;
+            tc_fence_after();
             const uint64_t a2 = umma_desc_sw128(kc_addr(s), 8192, 1024);
             const uint64_t b2 = umma_desc_mn<Cfg::kSw64>(uc_addr(s), Cfg::kUSub);
-            // MMA2 k step tt reads token rows 16 tt..16 tt+15 of v_decay, which the warps of
-            // quadrant tt write.  With M = K halves (K = 256: rows 128 m.. of k_c start 2 m
-            // sub-tiles in) each half accumulates its steps in the same order as before.
+            if (elect_one_sync()) {
+                // M = K halves (K = 256): rows 128 m.. of k_c start 2 m sub-tiles in
 #pragma unroll
-            for (int tt = 0; tt < 4; ++tt) {
-                if (!wait_warp(&vdec_ready[tt], static_cast<uint32_t>(c) & 1)) {
-                    go = false;
-                    break;
-                }
-                tc_fence_after();
-                if (elect_one_sync()) {
+                for (int m = 0; m < Cfg::kM2Halves; ++m)
 #pragma unroll
-                    for (int m = 0; m < Cfg::kM2Halves; ++m)
+                    for (int tt = 0; tt < 4; ++tt)
                         tc_mma_bf16(d2 + m * VT, a2 + static_cast<uint64_t>((m * 2 * 8192 + tt * 2048) >> 4),
                                     b2 + static_cast<uint64_t>((tt * 16 * Cfg::kRowB) >> 4), Cfg::kIdesc2,
                                     tt > 0 ? 1u : 0u);
-                    if (tt == 3) {
-                        tc_commit(mma2_done);
-                        tc_commit(&empty[s]);
-                    }
-                }
-                __syncwarp();
+                tc_commit(mma2_done);
+                tc_commit(&empty[s]);
             }
-            if (!go) break;
+            __syncwarp();
         }
         // Drain: every MMA this warp issued has completed before the TMEM it writes
         // is released (matters only on an abort path).
@@ -560,11 +526,12 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
 
         // kSharedH: the warps at even column slices issue the h stores of their sub-tile
         const bool h_issuer = !Cfg::kSharedH || (e & 1) == 0;
-        // kSharedH, issuer: wait until the quadrant's warps all wrote S_x (phase x of
-        // s_ready[q]), then store h[x]; false when the wait gave up
+        // kSharedH, issuer: wait until the epilogue warps all wrote S_x (phase x of
+        // s_ready; it cannot move on before this warp's next arrival), then store h[x];
+        // false when the wait gave up
         auto store_h_shared = [&](int64_t x) {
             bool go = true;
-            if (lane == 0) go = mbar_wait(&s_ready[q], static_cast<uint32_t>(x) & 1, ctl, 0x40);
+            if (lane == 0) go = mbar_wait(s_ready, static_cast<uint32_t>(x) & 1, ctl, 0x40);
             go = __shfl_sync(0xffffffffu, go ? 1 : 0, 0) != 0;
             if (go) store_h(x);
             return go;
@@ -576,11 +543,11 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
         tc_fence_before();
         __syncwarp();
         if constexpr (Cfg::kSharedH) {
-            if (lane == 0) mbar_arrive(&s_ready[q]);
+            if (lane == 0) mbar_arrive(s_ready);
             if (nchunks > 0 && h_issuer) ok = store_h_shared(0);
         } else {
             if (nchunks > 0) store_h(0);
-            if (lane == 0) mbar_arrive(&s_ready[q]);
+            if (lane == 0) mbar_arrive(s_ready);
         }
 
         for (int64_t c = 0; c < nchunks && ok; ++c) {
@@ -658,13 +625,12 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
                 for (int i = 0; i < kPairs; ++i) {
                     const int cb = i >> 3, j = (i >> 1) & 3, half = i & 1;
                     const float2 uu = unpack_bf16x2(uraw[i]);
-                    const __half2 ws = ref_gemm_to_f16x2(__uint_as_float(acc[cb][4 * j + 2 * half]),
-                                                         __uint_as_float(acc[cb][4 * j + 2 * half + 1]));
-                    const __half2 vn = __hsub2_rn(__floats2half2_rn(uu.x, uu.y), ws);
-                    vns[i] = h2_bits(vn);
-                    vds[i] = (half ? tb : ta) < len ? bf16x2_of_h2(__hmul2_rn(vn, half ? gb : ga)) : 0u;
+                    uint32_t vd;
+                    ref_vnew_vdecay_x2_fast(uu.x, uu.y, __uint_as_float(acc[cb][4 * j + 2 * half]),
+                                            __uint_as_float(acc[cb][4 * j + 2 * half + 1]), half ? gb : ga, vns[i], vd);
+                    vds[i] = (half ? tb : ta) < len ? vd : 0u;
                     if constexpr (!kDeferVnew) {
-                        const float2 f = __half22float2(vn);
+                        const float2 f = __half22float2(bits_h2(vns[i]));
                         vos[i] = (half ? tb : ta) < len ? pack_bf16x2(f.x, f.y) : 0u;
                     }
                 }
@@ -702,7 +668,7 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
             fence_proxy_async_smem();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&vdec_ready[q]);
+            if (lane == 0) mbar_arrive(vdec_ready);
             // v_new while MMA2 runs.
             const bool v_stored = p.v_new && !partial_varlen;
             if (kDeferVnew && p.v_new) {
@@ -884,13 +850,13 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
                 __syncwarp();
                 // MMA1 and the h store both only read the tile
                 if constexpr (Cfg::kSharedH) {
-                    if (lane == 0) mbar_arrive(&s_ready[q]);
+                    if (lane == 0) mbar_arrive(s_ready);
                     if (h_issuer && !store_h_shared(c + 1)) {
                         ok = false;
                         break;
                     }
                 } else {
-                    if (lane == 0) mbar_arrive(&s_ready[q]);
+                    if (lane == 0) mbar_arrive(s_ready);
                     store_h(c + 1);
                 }
             } else {

@@ -78,3 +78,32 @@ def test_epilogue2_pair_bits_equal(lib):
     out = _run(lib, 2, x)
     assert np.array_equal(out[:, 0], out[:, 2]), "state bits differ (first element)"
     assert np.array_equal(out[:, 1], out[:, 3]), "state bits differ (second element)"
+
+
+def test_epilogue1_fast_pair_bits_equal(lib):
+    """The chain without saturations, on its domain (|u|, |acc| < 16384, gate in [0, 1])."""
+    rng = np.random.default_rng(2)
+    x = _inputs(rng, 200_000)
+    x[:, 0:2] = _round_bf16(x[:, 0:2])
+    x[:, 4] = _round_f16(np.abs(np.tanh(x[:, 4])))
+    x[::7, 2] = x[::7, 0]
+    keep = np.all(np.abs(x[:, :4]) < 16384.0, axis=1)
+    out = _run(lib, 3, x[keep])
+    assert keep.sum() > 100_000
+    assert np.array_equal(out[:, 0], out[:, 2]), "v_new bits differ"
+    assert np.array_equal(out[:, 1], out[:, 3]), "v_decay bits differ"
+
+
+def test_epilogue2_fast_pair_bits_equal(lib):
+    """The state update without saturation, on its domain (finite state, |acc| < 32768,
+    alpha in [0, 1]); the state may exceed the f16 range (the conversion saturates it,
+    as the reference's cast does)."""
+    rng = np.random.default_rng(3)
+    x = _inputs(rng, 200_000)
+    x[:, 0:2] = _round_bf16(x[:, 0:2] * 2.0)
+    x[:, 4] = _round_f16(np.exp(-np.abs(x[:, 4]) / 1000.0))
+    keep = np.all(np.abs(x[:, 2:4]) < 32768.0, axis=1)
+    out = _run(lib, 4, x[keep])
+    assert keep.sum() > 100_000
+    assert np.array_equal(out[:, 0], out[:, 2]), "state bits differ (first element)"
+    assert np.array_equal(out[:, 1], out[:, 3]), "state bits differ (second element)"
