@@ -17,8 +17,17 @@
 //   epi1  v_new = u - D1 -> v_new tile (TMA store); v_dec = v_new*gate -> in place of u
 //   MMA2  D2[k,v] = sum_t k_c[t,k] v_dec[t,v]    M=K,  N=VT, K=64  (A, B MN-major)
 //   epi2  S = S*alpha + D2 (fp32 registers) -> bf16 S tile -> h[c+1] (TMA store)
-// All shared-memory tiles use the 128-byte swizzle, in 64-column (128 B)
-// sub-tiles, so one layout serves the TMA boxes and the UMMA descriptors.
+// The shared-memory tiles use the 128-byte swizzle in 64-column (128 B) sub-tiles,
+// or (32-column tiles) the 64-byte swizzle, so one layout serves the TMA boxes and
+// the UMMA descriptors.
+//
+// The K tile K_ is 64, 128 or 256; a caller's K below it arrives zero-filled from
+// the tensor maps (rows past K of the state stay zero and are never stored).  With
+// K_ = 256, MMA2 runs as two M = 128 halves into separate TMEM column ranges and
+// epilogue warp w owns state rows 128 (w / 4) + 32 (w % 4) + lane.  Warps whose
+// column slice is narrower than a 64-column sub-tile stage v_new in regions of
+// their own (kSplitVout); with the reference arithmetic's sixteen-warp 128-column
+// tiles the h store of a sub-tile is shared by two warps (kSharedH).
 //
 // Every wait is bounded (WaitCtl); on expiry the CTA raises its abort flag,
 // records the role in the status word, drains its own copies and returns.
