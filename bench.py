@@ -24,8 +24,16 @@ bytes per launch to the measured HBM copy bandwidth.  ``cpu_baseline`` is
 the reference's arithmetic (the CPU oracle, a restatement of the reference
 PyTorch code) timed on this host's cores on a bounded sample.
 
+``parity`` is the same CPU oracle used as the checker of the last timed output
+(sequence 0, two heads; rank 0, untimed).  ``strong_scaling`` times the
+multi-GPU configuration (B=8, T=8192, H=64, K=128, V=256) with its heads split
+over the ranks, after the headline and outside its timed region; rank 0 also
+times the unsplit configuration.  ``e2e.copy_only_ms_per_step`` moves the e2e
+step's bytes with no kernel, which names what bounds the e2e number.
+
 ``--impl reference`` times that CPU implementation alone (rank 0; other
-ranks exit), as the reference arm.
+ranks exit), as the reference arm: the whole job per step where it fits a few
+seconds.
 """
 
 from __future__ import annotations
