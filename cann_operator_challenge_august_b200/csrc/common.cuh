@@ -245,6 +245,18 @@ __device__ __forceinline__ void ref_state_x2_fast(float& s0, float& s1, uint32_t
     s1 = __high2float(sum);
 }
 
+// The same on bf16 bits: the state pair in, the new state pair out (no unpacking of
+// the bf16x2 sum).
+__device__ __forceinline__ uint32_t ref_state_bits_fast(uint32_t s_bits, uint32_t up, __half2 alpha)
+{
+    const __half2 sh = bits_h2(f16x2_satfinite(__uint_as_float(s_bits << 16), __uint_as_float(s_bits & 0xffff0000u)));
+    const __half2 hd = __hmul2_rn(sh, alpha);
+    const uint32_t hb = bf16x2_of_h2(hd), ub = bf16x2_of_h2(bits_h2(up));
+    const __nv_bfloat162 sum =
+        __hadd2_rn(*reinterpret_cast<const __nv_bfloat162*>(&hb), *reinterpret_cast<const __nv_bfloat162*>(&ub));
+    return *reinterpret_cast<const uint32_t*>(&sum);
+}
+
 // max that propagates NaN (so a NaN operand fails a later `< bound` test)
 __device__ __forceinline__ float fmax_nan(float a, float b)
 {

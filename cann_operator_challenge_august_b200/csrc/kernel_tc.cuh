@@ -194,6 +194,8 @@ struct StateRegs {
         else
             return pack_bf16x2(f[i], f[i + 1]);
     }
+    // bf16 bits of values i, i + 1 (i even; packed only)
+    __device__ __forceinline__ void set_pair_bits(int i, uint32_t bits) { b[i >> 1] = bits; }
     // values i, i + 1 (i even); rounded to bf16 when packed
     __device__ __forceinline__ void set_pair(int i, float lo, float hi)
     {
@@ -802,11 +804,15 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
 #pragma unroll
                             for (int i = 0; i < 16; i += 2) {
                                 const int si2 = 32 * cb + 16 * j + i;
-                                float s0 = st.get(si2), s1 = st.get(si2 + 1);
-                                ref_state_x2_fast(s0, s1, h2_bits(ref_gemm_to_f16x2(__uint_as_float(r[j][i]),
-                                                                                    __uint_as_float(r[j][i + 1]))),
-                                                  ah);
-                                st.set_pair(si2, s0, s1);
+                                const uint32_t up = h2_bits(ref_gemm_to_f16x2(__uint_as_float(r[j][i]),
+                                                                              __uint_as_float(r[j][i + 1])));
+                                if constexpr (REF) {
+                                    st.set_pair_bits(si2, ref_state_bits_fast(st.pair_bits(si2), up, ah));
+                                } else {
+                                    float s0 = st.get(si2), s1 = st.get(si2 + 1);
+                                    ref_state_x2_fast(s0, s1, up, ah);
+                                    st.set_pair(si2, s0, s1);
+                                }
                             }
                     } else {
                         if constexpr (REF) state_recheck = true;

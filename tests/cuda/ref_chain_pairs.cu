@@ -71,6 +71,22 @@ __global__ void epi2_pairs_fast(const float* in, uint32_t* out, int n)
     out[4 * i + 3] = __float_as_uint(p1);
 }
 
+// in: [n][5] = s0, s1 (bf16 values), a0, a1, alpha -> out: scalar s0', s1', then the fp32 values
+// of the bf16 pair ref_state_bits_fast returns
+__global__ void epi2_pairs_bits(const float* in, uint32_t* out, int n)
+{
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const float* x = in + 5 * i;
+    const __nv_bfloat162 sb = __floats2bfloat162_rn(x[0], x[1]);
+    const uint32_t r = ref_state_bits_fast(*reinterpret_cast<const uint32_t*>(&sb),
+                                           h2_bits(ref_gemm_to_f16x2(x[2], x[3])), __float2half2_rn(x[4]));
+    out[4 * i + 0] = __float_as_uint(ref_state(x[0], x[4], x[2]));
+    out[4 * i + 1] = __float_as_uint(ref_state(x[1], x[4], x[3]));
+    out[4 * i + 2] = r << 16;
+    out[4 * i + 3] = r & 0xffff0000u;
+}
+
 extern "C" int run_pairs(int which, const float* host_in, uint32_t* host_out, int n)
 {
     float* din = nullptr;
@@ -84,8 +100,10 @@ extern "C" int run_pairs(int which, const float* host_in, uint32_t* host_out, in
         epi2_pairs<<<(n + 255) / 256, 256>>>(din, dout, n);
     else if (which == 3)
         epi1_pairs_fast<<<(n + 255) / 256, 256>>>(din, dout, n);
-    else
+    else if (which == 4)
         epi2_pairs_fast<<<(n + 255) / 256, 256>>>(din, dout, n);
+    else
+        epi2_pairs_bits<<<(n + 255) / 256, 256>>>(din, dout, n);
     cudaError_t e = cudaDeviceSynchronize();
     cudaMemcpy(host_out, dout, sizeof(uint32_t) * 4 * n, cudaMemcpyDeviceToHost);
     cudaFree(din);

@@ -103,7 +103,8 @@ def test_epilogue2_fast_pair_bits_equal(lib):
     x[:, 0:2] = _round_bf16(x[:, 0:2] * 2.0)
     x[:, 4] = _round_f16(np.exp(-np.abs(x[:, 4]) / 1000.0))
     keep = np.all(np.abs(x[:, 2:4]) < 32768.0, axis=1)
-    out = _run(lib, 4, x[keep])
-    assert keep.sum() > 100_000
-    assert np.array_equal(out[:, 0], out[:, 2]), "state bits differ (first element)"
-    assert np.array_equal(out[:, 1], out[:, 3]), "state bits differ (second element)"
+    for which in (4, 5):  # fp32 pair in and out; bf16 pair bits in and out
+        out = _run(lib, which, x[keep])
+        assert keep.sum() > 100_000
+        assert np.array_equal(out[:, 0], out[:, 2]), f"state bits differ (first element, form {which})"
+        assert np.array_equal(out[:, 1], out[:, 3]), f"state bits differ (second element, form {which})"
