@@ -302,26 +302,6 @@ def cpu_time(sample, threads):
     return time.perf_counter() - t0
 
 
-def cpu_reference_rate(c, budget_s, n_threads, max_pairs=None):
-    """Time the CPU oracle (reference arithmetic) on a bounded sample of the
-    workload: P (sequence, head) pairs x C chunks.  Returns (tokens/s for the
-    whole job, description, threads)."""
-    # every host core this process may run on (torchrun sets OMP_NUM_THREADS=1 for its ranks)
-    threads = n_threads or len(os.sched_getaffinity(0))
-    P = max(1, min(threads, max_pairs or threads, c["B"] * c["H"]))
-    NT = (c["T"] + 63) // 64
-    t1 = cpu_time(cpu_sample(c, P, 1), threads)
-    chunks = int(max(1, min(NT, budget_s / max(t1, 1e-4))))
-    dt = cpu_time(cpu_sample(c, P, chunks), threads)
-    pair_chunks_per_s = P * chunks / dt
-    job_pair_chunks = c["B"] * c["H"] * NT
-    tokens = c["B"] * c["T"]
-    rate = tokens * pair_chunks_per_s / job_pair_chunks
-    desc = (f"{P} (sequence, head) pairs x {chunks} chunks of the workload ({P * chunks} of "
-            f"{job_pair_chunks} pair-chunks, {dt:.2f} s), scaled linearly to the whole job")
-    return rate, desc, threads
-
-
 def cpu_parity_check(c, inp, out, numerics, heads=None):
     """The CPU oracle as the checker of one timed output (outside every timed
     region): sequence 0 and two heads, against the arithmetic the bench ran and
@@ -474,35 +454,44 @@ def copy_only_ms(host_in, host_out, dev, steps, world):
     return max_over_ranks(e0.elapsed_time(e1) / steps, world)
 
 
-def run_reference_arm(args, cfg_name, c, world, rank):
-    """The reference arm: the CPU implementation of the path on this host's cores.
-    Each step runs the whole job (every (sequence, head) pair, every chunk) when
-    that fits about 3 s, so ms_per_step is the measured time of a step; a larger
-    job runs a fixed subset of pairs per step and says so."""
-    if rank != 0:
-        return 0
-    K, W = args.steps, args.warmup
+def cpu_reference_steps(c, steps, warmup, per_step_s):
+    """The CPU oracle (reference arithmetic) with every host thread, `steps` timed
+    steps after `warmup`: each step runs the whole job (every (sequence, head)
+    pair, every chunk) when that fits `per_step_s`, else a fixed subset of pairs
+    (named in the description).  Returns (tokens/s, seconds per step, fraction of
+    the job per step, description, threads)."""
     threads = len(os.sched_getaffinity(0))
     NT = (c["T"] + 63) // 64
     pairs = c["B"] * c["H"]
     probe = cpu_time(cpu_sample(c, min(threads, pairs), 1), threads)
     est_pair_chunk_s = probe / min(threads, pairs) * threads  # wall time of `threads` pair-chunks in parallel
-    per_step = max(0.5, min(3.0, 150.0 / max(1, K + W)))
     P = pairs
-    while P > threads and est_pair_chunk_s * (P / threads) * NT > per_step:
+    while P > threads and est_pair_chunk_s * (P / threads) * NT > per_step_s:
         P = max(threads, P // 2)
     sample = cpu_sample(c, P, NT)
     times = []
-    for i in range(W + K):
+    for i in range(warmup + steps):
         dt = cpu_time(sample, threads)
-        if i >= W:
+        if i >= warmup:
             times.append(dt)
     step_s = statistics.median(times)
     frac = P / pairs
     value = c["B"] * c["T"] * frac / step_s
     desc = (f"{P} of {pairs} (sequence, head) pairs x all {NT} chunks per step"
             + ("" if P == pairs else f" ({frac:.3f} of the job; tokens/s counts that fraction of B*T)")
-            + f", median of {K} steps after {W} warm-up steps, {threads} threads")
+            + f", median of {steps} steps after {warmup} warm-up steps, {threads} threads")
+    return value, step_s, frac, desc, threads
+
+
+def run_reference_arm(args, cfg_name, c, world, rank):
+    """The reference arm: the CPU implementation of the path on this host's cores.
+    Each step runs the whole job when that fits about 3 s, so ms_per_step is the
+    measured time of a step; a larger job runs a fixed subset of pairs per step
+    and says so."""
+    if rank != 0:
+        return 0
+    K, W = args.steps, args.warmup
+    value, step_s, frac, desc, threads = cpu_reference_steps(c, K, W, max(0.5, min(3.0, 150.0 / max(1, K + W))))
     line = {
         "impl": "reference",
         "metric": "fwd_h tokens/s",
@@ -706,7 +695,7 @@ def main() -> int:
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        rate, desc, threads = cpu_reference_rate(c, 12.0, 0)
+        rate, _, _, desc, threads = cpu_reference_steps(c, 3, 1, 3.0)
         cpu = {"value": rate, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": desc}
 
     if rank == 0:
