@@ -4,7 +4,7 @@
 // reference's ProcessTask, op_kernel/chunk_gated_delta_rule_fwd_h.h:421-510).
 // The two per-chunk contractions run as CUDA-core FMAs from shared memory.
 // It serves shapes and dtypes the tensor-core kernel does not cover (fp32
-// I/O, K not in {64, 128}, strides TMA cannot describe).
+// I/O, K or V not a multiple of 8, strides TMA cannot describe).
 #pragma once
 
 #include "common.cuh"
