@@ -554,6 +554,7 @@ def main() -> int:
     ap.add_argument("--config", choices=sorted(CONFIGS), default="ns")
     ap.add_argument("--numerics", choices=["fp32_state", "reference"], default="fp32_state")
     ap.add_argument("--v-tile", type=int, default=0)
+    ap.add_argument("--chains", type=int, default=0, help="chains per CTA (0: the planner's choice)")
     ap.add_argument("--gdr-path", choices=["auto", "fused", "three_kernels"], default="auto",
                     help="--op gdr: the recurrence and output kernels (default: the planner's choice)")
     ap.add_argument("--e2e-steps", type=int, default=5)
@@ -589,7 +590,7 @@ def main() -> int:
     c = shard(cfg, world, rank)
     inp = gen_inputs(c, seed=1000 + rank, device=dev)
     stream = torch.cuda.current_stream(dev)
-    opts = dict(numerics=args.numerics, v_tile=args.v_tile)
+    opts = dict(numerics=args.numerics, v_tile=args.v_tile, chains=args.chains)
 
     def step():
         return cg.chunk_gated_delta_rule_fwd_h(inp["k"], inp["w"], inp["u"], inp["g"], inp["initial_state"],

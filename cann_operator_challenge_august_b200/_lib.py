@@ -88,7 +88,7 @@ class CgdrFwdHOptions(ctypes.Structure):
         ("v_tile", ctypes.c_int32),
         ("wait_timeout_ms", ctypes.c_int32),
         ("fault_inject", ctypes.c_int32),
-        ("reserved", ctypes.c_int32),
+        ("chains", ctypes.c_int32),
     ]
 
 
@@ -114,7 +114,7 @@ class CgdrFwdHPlan(ctypes.Structure):
         (n, ctypes.c_int32) for n in (
             "has_initial_state", "is_varlen", "store_final_state", "save_new_value", "plan_key",
             "kernel", "grid", "block", "smem_bytes", "stages", "numerics", "layout")] + [
-        ("workspace_bytes", ctypes.c_uint64)]
+        ("workspace_bytes", ctypes.c_uint64), ("chains", ctypes.c_int32), ("reserved", ctypes.c_int32)]
 
     def as_dict(self) -> dict:
         return {name: getattr(self, name) for name, _ in self._fields_}

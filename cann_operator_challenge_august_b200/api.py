@@ -97,7 +97,7 @@ class ChunkGatedDeltaRuleFwdH:
     def __init__(self, k, w, u, g, initial_state, cu_seqlens, chunk_indices, chunk_size, h, v, final_state,
                  *, chunk_offsets=None, layout="head_major", numerics="reference",
                  strict_reference_limits=False, force_kernel=0, v_tile=0, wait_timeout_ms=0, fault_inject=0,
-                 extended=True):
+                 chains=0, extended=True):
         lib = _lib.load()
         self._keep = (k, w, u, g, initial_state, cu_seqlens, chunk_indices, chunk_offsets, h, v, final_state)
         ws = ctypes.c_uint64(0)
@@ -109,7 +109,7 @@ class ChunkGatedDeltaRuleFwdH:
                 layout=_lib.LAYOUT_HEAD_MAJOR if layout == "head_major" else _lib.LAYOUT_TOKEN_MAJOR,
                 numerics=_lib.NUMERICS[numerics], strict_reference_limits=int(strict_reference_limits),
                 force_kernel=int(force_kernel), v_tile=int(v_tile), wait_timeout_ms=int(wait_timeout_ms),
-                fault_inject=int(fault_inject))
+                fault_inject=int(fault_inject), chains=int(chains))
             st = lib.cgdrChunkGatedDeltaRuleFwdHGetWorkspaceSizeEx(
                 *[ctypes.byref(d) for d in descs], ctypes.byref(_desc(chunk_offsets)), int(chunk_size),
                 *[ctypes.byref(d) for d in outs], ctypes.byref(opt), ctypes.byref(ws), ctypes.byref(ex))

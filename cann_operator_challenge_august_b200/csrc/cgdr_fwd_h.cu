@@ -317,6 +317,24 @@ cgdrStatus build(const cgdrTensor* k, const cgdrTensor* w, const cgdrTensor* u, 
             delete ex_;
             return fail(CGDR_STATUS_UNSUPPORTED, "v_tile 32 needs 64 < K <= 128");
         }
+        // Two chains per CTA (each column half of the V tile a chain of its own) are
+        // built for the K tile 128 with 32- and 128-column tiles.  The automatic plan
+        // takes them for the reference arithmetic, whose heavier epilogues then run
+        // while the other chain's MMAs do: B=1 T=65536 H=32 1.485 against 1.597 ms,
+        // B=4 T=8192 H=32 0.459 against 0.467 ms (sixteen-warp single chain).  The
+        // fp32-state chain is bound by the MMA hand-offs, and two chains there only
+        // contend for the tensor pipe (1.134 against 1.089 ms; 0.283 against 0.273 ms).
+        const bool two_chain_tile = kt == 128 && (vt == 32 || vt == 128);
+        const int chains = opt.chains != 0 ? opt.chains : (ref && two_chain_tile ? 2 : 1);
+        if (chains != 1 && chains != 2) {
+            delete ex_;
+            return fail(CGDR_STATUS_UNSUPPORTED, "chains must be 0 (auto), 1 or 2");
+        }
+        if (chains == 2 && !two_chain_tile) {
+            delete ex_;
+            return fail(CGDR_STATUS_UNSUPPORTED, "two chains per CTA need 64 < K <= 128 and v_tile 32 or 128");
+        }
+        pl.chains = chains;
         if (kt == 256 && vt != 64) {
             delete ex_;
             return fail(CGDR_STATUS_UNSUPPORTED, "K > 128 runs 64-column V tiles only");
@@ -328,6 +346,7 @@ cgdrStatus build(const cgdrTensor* k, const cgdrTensor* w, const cgdrTensor* u, 
         // warps (four 32-column quarters per lane quadrant): its epilogues issue about twice
         // the instructions of the fp32-state ones.
         pl.block = kt == 256                      ? TcConfig<256, 64, 2, 2>::kThreads
+                   : chains == 2                  ? TcConfig<128, 32, 3, 2, 2>::kThreads  // 11 warps (either width)
                    : (vt == 128 && kt == 128 && ref) ? TcConfig<128, 128, 3, 4>::kThreads
                    : vt == 128                    ? TcConfig<128, 128, 3, 2>::kThreads
                                                   : TcConfig<128, 64, 2, 1>::kThreads;
@@ -342,22 +361,27 @@ cgdrStatus build(const cgdrTensor* k, const cgdrTensor* w, const cgdrTensor* u, 
         pl.block = kSimtThreads;
         pl.smem_bytes = static_cast<int32_t>(simt_smem_bytes(static_cast<int>(d.K)));
     }
+    if (pl.chains == 0) pl.chains = 1;
     pl.v_tile_count = (d.V + pl.v_tile - 1) / pl.v_tile;
-    pl.task_count = d.N * d.HV * pl.v_tile_count;
-    pl.grid = static_cast<int32_t>(pl.task_count);
+    // a CTA runs one V tile: one chain, or two of half its width
+    pl.task_count = d.N * d.HV * pl.v_tile_count * pl.chains;
+    pl.grid = static_cast<int32_t>(d.N * d.HV * pl.v_tile_count);
     p.v_tile = static_cast<int32_t>(pl.v_tile);
     p.n_vtiles = static_cast<int32_t>(pl.v_tile_count);
     if (pl.kernel == 1) {
 #define CGDR_SMEM(K_, VT_, ST_, EW_) TcConfig<K_, VT_, ST_, EW_>::kSmemBytes
+#define CGDR_SMEM2(K_, VT_) TcConfig<K_, VT_, 3, 2, 2>::kSmemBytes
         if (kt == 256)
             pl.smem_bytes = CGDR_SMEM(256, 64, 2, 2);
         else if (kt == 128)
-            pl.smem_bytes = pl.v_tile == 128  ? (ref ? CGDR_SMEM(128, 128, 3, 4) : CGDR_SMEM(128, 128, 3, 2))
-                            : pl.v_tile == 64 ? CGDR_SMEM(128, 64, 2, 1)
-                                              : CGDR_SMEM(128, 32, 3, 1);
+            pl.smem_bytes = pl.chains == 2    ? (pl.v_tile == 128 ? CGDR_SMEM2(128, 128) : CGDR_SMEM2(128, 32))
+                            : pl.v_tile == 128 ? (ref ? CGDR_SMEM(128, 128, 3, 4) : CGDR_SMEM(128, 128, 3, 2))
+                            : pl.v_tile == 64  ? CGDR_SMEM(128, 64, 2, 1)
+                                               : CGDR_SMEM(128, 32, 3, 1);
         else
             pl.smem_bytes = pl.v_tile == 128 ? CGDR_SMEM(64, 128, 3, 2) : CGDR_SMEM(64, 64, 2, 1);
 #undef CGDR_SMEM
+#undef CGDR_SMEM2
     }
     uint64_t ws = kHeaderBytes;
     if (has_cu) ws += align256(4 * static_cast<uint64_t>(d.N + 1)) + align256(4 * static_cast<uint64_t>(d.N));
@@ -386,10 +410,12 @@ cgdrStatus build_maps(const cgdrExecutor* ex, TcMaps* m)
         const uint32_t box[4] = {64, 1, 64, 1};
         if ((st = make_map(&m->w, const_cast<void*>(p.w), 4, size, stride, box, "w"))) return st;
     }
-    // 32-column tiles move u, v_new and h in 32-column boxes with the 64-byte swizzle
-    const bool sw64 = ex->plan.v_tile == 32;
-    const uint32_t cols = sw64 ? 32 : 64;
-    const int swz = sw64 ? 64 : 128;
+    // 32-column tiles move u, v_new and h in 32-column boxes with the 64-byte swizzle,
+    // the two 16-column chains in 16-column boxes with the 32-byte swizzle
+    const bool sw32 = ex->plan.v_tile == 32 && ex->plan.chains == 2;
+    const bool sw64 = ex->plan.v_tile == 32 && !sw32;
+    const uint32_t cols = sw32 ? 16 : sw64 ? 32 : 64;
+    const int swz = sw32 ? 32 : sw64 ? 64 : 128;
     {
         const int64_t size[4] = {p.V, p.H, p.T, p.B}, stride[4] = {1, p.u_sh, p.u_st, p.u_sb};
         const uint32_t box[4] = {cols, 1, 64, 1};
@@ -399,8 +425,8 @@ cgdrStatus build_maps(const cgdrExecutor* ex, TcMaps* m)
         // the K tile 256 kernel stages v_new per warp in 32-column regions (64-byte swizzle)
         const bool v32 = sw64 || tc_k_tile(p.K) == 256 || tc_quarters(ex->plan);
         const int64_t size[4] = {p.V, p.H, p.T, p.B}, stride[4] = {1, p.v_sh, p.v_st, p.v_sb};
-        const uint32_t box[4] = {v32 ? 32u : 64u, 1, 16, 1};
-        if ((st = make_map(&m->v, p.v_new, 4, size, stride, box, "v", v32 ? 64 : 128))) return st;
+        const uint32_t box[4] = {sw32 ? 16u : v32 ? 32u : 64u, 1, 16, 1};
+        if ((st = make_map(&m->v, p.v_new, 4, size, stride, box, "v", sw32 ? 32 : v32 ? 64 : 128))) return st;
     } else {
         memset(&m->v, 0, sizeof(m->v));
     }
@@ -412,22 +438,22 @@ cgdrStatus build_maps(const cgdrExecutor* ex, TcMaps* m)
     return CGDR_STATUS_SUCCESS;
 }
 
-template <int K_, int VT, int STAGES, int EW, bool REF>
+template <int K_, int VT, int STAGES, int EW, bool REF, int CH = 1>
 cudaError_t launch_tc(const TcArgs& args, int grid, cudaStream_t stream)
 {
-    using Cfg = TcConfig<K_, VT, STAGES, EW>;
-    auto kern = fwd_h_tc_kernel<K_, VT, STAGES, EW, REF>;
+    using Cfg = TcConfig<K_, VT, STAGES, EW, CH>;
+    auto kern = fwd_h_tc_kernel<K_, VT, STAGES, EW, REF, CH>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
     if (e != cudaSuccess) return e;
     kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(args);
     return cudaGetLastError();
 }
 
-template <int K_, int VT, int STAGES, int EW>
+template <int K_, int VT, int STAGES, int EW, int CH = 1>
 cudaError_t launch_tc_numerics(const TcArgs& args, int grid, cudaStream_t stream)
 {
-    return args.p.numerics == 0 ? launch_tc<K_, VT, STAGES, EW, true>(args, grid, stream)
-                                : launch_tc<K_, VT, STAGES, EW, false>(args, grid, stream);
+    return args.p.numerics == 0 ? launch_tc<K_, VT, STAGES, EW, true, CH>(args, grid, stream)
+                                : launch_tc<K_, VT, STAGES, EW, false, CH>(args, grid, stream);
 }
 
 }  // namespace
@@ -541,6 +567,9 @@ cgdrStatus fwd_h_enqueue(const cgdrExecutor* executor, int* status, uint8_t* met
         const int kt = tc_k_tile(p.K);
         if (kt == 256)
             e = launch_tc_numerics<256, 64, 2, 2>(args, grid, stream);
+        else if (kt == 128 && pl.chains == 2)
+            e = pl.v_tile == 128 ? launch_tc_numerics<128, 128, 3, 2, 2>(args, grid, stream)
+                                 : launch_tc_numerics<128, 32, 3, 2, 2>(args, grid, stream);
         else if (kt == 128 && tc_quarters(pl))
             e = launch_tc<128, 128, 3, 4, true>(args, grid, stream);
         else if (kt == 128)

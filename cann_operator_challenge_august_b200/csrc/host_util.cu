@@ -54,7 +54,9 @@ cgdrStatus make_map(CUtensorMap* map, void* base, int rank, const int64_t* size,
     for (int i = 1; i < rank; ++i) gstride[i - 1] = static_cast<cuuint64_t>(stride[i]) * 2;
     const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, base, gdim, gstride, bdim, estride,
                           CU_TENSOR_MAP_INTERLEAVE_NONE,
-                          swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
+                          swizzle_bytes == 32   ? CU_TENSOR_MAP_SWIZZLE_32B
+                          : swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                : CU_TENSOR_MAP_SWIZZLE_128B,
                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(CGDR_STATUS_CUDA_ERROR, "cuTensorMapEncodeTiled(%s) failed: %d", name, (int)r);
     return CGDR_STATUS_SUCCESS;

@@ -57,7 +57,7 @@ inline bool tma_aligned(const cgdrTensor* t)
     return true;
 }
 
-// A bf16 tensor map with 128-byte swizzle (64-byte with swizzle_bytes = 64) over `rank` dims given innermost
+// A bf16 tensor map with 128-byte swizzle (64- or 32-byte with swizzle_bytes = 64 or 32) over `rank` dims given innermost
 // first (sizes in elements, strides in elements for dims 1..rank-1).
 cgdrStatus make_map(CUtensorMap* map, void* base, int rank, const int64_t* size, const int64_t* stride,
                     const uint32_t* box, const char* name, int swizzle_bytes = 128);

@@ -5,12 +5,16 @@
 // ProcessTask (op_kernel/chunk_gated_delta_rule_fwd_h.h:421-510), with the
 // state resident on chip instead of bounced through global memory.
 //
-// Warp roles (block = 32 * (4*EW + 2) threads):
+// Warp roles (block = 32 * (4*EW + 1 + chains) threads):
 //   warps 0 .. 4*EW-1  epilogue: warp w reads TMEM lane quadrant w%4 and the
 //                      column slice (w/4) of width VT/EW;
 //   warp 4*EW          TMA producer: k_c, w_c, u_c of chunk c into a ring of
 //                      STAGES shared-memory stages;
-//   warp 4*EW+1        MMA issuer and TMEM owner.
+//   warp 4*EW+1 (+c)   MMA issuer of chain c; the first one owns TMEM.
+// Usually the CTA's VT columns are one chain.  With CH = 2 (K tile 128, VT = 32 or
+// 128, EW = 2) each column slice of VT / 2 is a chain of its own: its own MMAs
+// (N = VT / 2), TMEM accumulators, state sub-tile and barriers, with only the load
+// stages shared, so that one chain's epilogues run while the other's MMAs do.
 //
 // Per chunk c (S = state before the chunk, bf16 copy in shared memory):
 //   MMA1  D1[t,v] = sum_k w_c[t,k] S[k,v]        M=64, N=VT, K=K   (A K-major, B MN-major)
@@ -18,8 +22,9 @@
 //   MMA2  D2[k,v] = sum_t k_c[t,k] v_dec[t,v]    M=K,  N=VT, K=64  (A, B MN-major)
 //   epi2  S = S*alpha + D2 (fp32 registers) -> bf16 S tile -> h[c+1] (TMA store)
 // The shared-memory tiles use the 128-byte swizzle in 64-column (128 B) sub-tiles,
-// or (32-column tiles) the 64-byte swizzle, so one layout serves the TMA boxes and
-// the UMMA descriptors.
+// or (32-column tiles) the 64-byte swizzle, or (two 16-column chains) the 32-byte
+// swizzle in 16-column sub-tiles, so one layout serves the TMA boxes and the UMMA
+// descriptors.
 //
 // The K tile K_ is 64, 128 or 256; a caller's K below it arrives zero-filled from
 // the tensor maps (rows past K of the state stay zero and are never stored).  With
@@ -51,26 +56,33 @@ struct TcArgs {
     FwdHParams p;
 };
 
-template <int K_, int VT, int STAGES, int EW>
+template <int K_, int VT, int STAGES, int EW, int CH = 1>
 struct TcConfig {
     static_assert(K_ == 64 || K_ == 128 || K_ == 256, "tensor-core path: K tile in {64, 128, 256}");
     static_assert(VT == 32 || VT == 64 || VT == 128, "tensor-core path: V tile in {32, 64, 128}");
-    static_assert(EW == 1 || EW == VT / 64 || (K_ == 256 && VT == 64 && EW == 2) || (K_ == 128 && VT == 128 && EW == 4),
-                  "column split must be 1, one warp per 64-column sub-tile, (K = 256) two 32-column halves, or "
-                  "(K = 128, VT = 128) four 32-column quarters");
+    static_assert(EW == 1 || EW == VT / 64 || (K_ == 256 && VT == 64 && EW == 2) || (K_ == 128 && VT == 128 && EW == 4) ||
+                      (K_ == 128 && VT == 32 && EW == 2 && CH == 2),
+                  "column split must be 1, one warp per 64-column sub-tile, (K = 256) two 32-column halves, "
+                  "(K = 128, VT = 128) four 32-column quarters or (K = 128, VT = 32) two 16-column chains");
+    static_assert(CH == 1 || (CH == 2 && EW == 2 && K_ == 128 && (VT == 32 || VT == 128)),
+                  "two chains per CTA: K tile 128, VT 32 or 128, one column slice each");
     static_assert(VT != 32 || K_ == 128, "32-column tiles: K = 128");
     static_assert(K_ != 256 || VT == 64, "K = 256: 64-column tiles");
-    // 32-column tiles keep u_c, v_new and S in 64-byte rows (64-byte swizzle);
-    // wider tiles in 64-column sub-tiles of 128-byte rows (128-byte swizzle)
-    static constexpr bool kSw64 = VT == 32;
-    static constexpr int kRowB = kSw64 ? 64 : 128;      // bytes per row of a u_c / v_new / S sub-tile
-    static constexpr int kSubCols = kSw64 ? 32 : 64;     // columns per sub-tile
+    // each column slice a chain of its own (CH = 2), or one chain
+    static constexpr int kChains = CH;
+    // Swizzle of the u_c / v_new / S tiles: the two 16-column chains keep them in
+    // 16-column sub-tiles of 32-byte rows, 32-column tiles in 64-byte rows, wider
+    // tiles in 64-column sub-tiles of 128-byte rows.
+    static constexpr int kSwz = VT == 32 ? (kChains == 2 ? 32 : 64) : 128;
+    static constexpr int kRowB = kSwz;                  // bytes per row of a u_c / v_new / S sub-tile
+    static constexpr int kSubCols = kSwz / 2;           // columns per sub-tile
     static constexpr int kUSub = 64 * kRowB;            // one sub-tile of u_c / v_new (64 token rows)
     static constexpr int kEpiWarps = 4 * EW;
-    static constexpr int kThreads = 32 * (kEpiWarps + 2);
+    static constexpr int kThreads = 32 * (kEpiWarps + 1 + kChains);
     static constexpr int kProducerWarp = kEpiWarps;
-    static constexpr int kMmaWarp = kEpiWarps + 1;
+    static constexpr int kMmaWarp = kEpiWarps + 1;      // chain c's MMA issuer: kMmaWarp + c
     static constexpr int kCW = VT / EW;                 // columns per epilogue warp
+    static constexpr int kChainCols = VT / kChains;     // columns of one chain (N of its MMAs)
     static constexpr int kSubK = K_ / 64;              // 64-column sub-tiles of k_c / w_c
     static constexpr int kSubV = VT / kSubCols;         // sub-tiles of u_c / S / v_new
     static constexpr int kTileKBytes = K_ * 128;       // [64 tokens][K] bf16
@@ -83,7 +95,8 @@ struct TcConfig {
     static constexpr int kOffVout = kOffS + kSBytes;
     static constexpr int kOffG = kOffVout + kVoutBytes;  // [STAGES][64] fp32 gate inputs
     static constexpr int kOffBar = kOffG + STAGES * 64 * 4;
-    static constexpr int kNumBars = 2 * STAGES + 9;  // + mma1/2_done, drain, s_ready, vdec_ready, h_read[4]
+    // full/empty per stage; per chain mma1_done, mma2_done, drain, s_ready, vdec_ready; h_read[4]
+    static constexpr int kNumBars = 2 * STAGES + 5 * kChains + 4;
     static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;  // + tmem slot, abort flag, alignment
     static constexpr uint32_t kStageTx = kStageBytes;
     // MMA2 (M = K) as M = 128 halves when K = 256: D2 rows [128 m, 128 m + 128) at TMEM
@@ -109,8 +122,8 @@ struct TcConfig {
     static constexpr bool kSharedH = K_ >= 128 && kE2Cols < kSubCols;
     static constexpr int kVoutRegion = 64 * 64;  // bytes of one warp's region (64 rows x 64 B)
     static constexpr int kMinBlocks = (VT == 64 && K_ != 256) ? 2 : 1;  // CTAs resident per SM the tile is sized for
-    static constexpr uint32_t kIdesc1 = umma_idesc_bf16(64, VT, false, true);
-    static constexpr uint32_t kIdesc2 = umma_idesc_bf16(kM2, VT, true, true);
+    static constexpr uint32_t kIdesc1 = umma_idesc_bf16(64, kChainCols, false, true);
+    static constexpr uint32_t kIdesc2 = umma_idesc_bf16(kM2, kChainCols, true, true);
 };
 
 // Byte offset of element (row, col) inside a swizzled tile made of 64-column
@@ -121,23 +134,29 @@ __device__ __forceinline__ uint32_t sw128_off(int row, int col, int sub_bytes)
     return sub * sub_bytes + row * 128 + ((((cc >> 3) ^ (row & 7)) & 7) << 4) + ((cc & 7) << 1);
 }
 
-// Byte offset of element (row, col) of a u_c / v_new / S tile: 128-byte swizzle in
-// 64-column sub-tiles, or (SW64) one 32-column tile of 64-byte rows whose
-// 16-byte chunks are XORed with (row / 2) % 4.
-template <bool SW64>
+// Byte offset of element (row, col) of a u_c / v_new / S tile (SWZ = swizzle bytes):
+//   128  64-column sub-tiles of 128-byte rows (sw128_off);
+//    64  one 32-column tile of 64-byte rows, 16-byte chunks XORed with (row / 2) % 4;
+//    32  16-column sub-tiles of 32-byte rows, 16-byte chunks XORed with (row / 4) % 2.
+template <int SWZ>
 __device__ __forceinline__ uint32_t tile_off(int row, int col, int sub_bytes)
 {
-    if constexpr (SW64)
+    if constexpr (SWZ == 32)
+        return (col >> 4) * sub_bytes + row * 32 + ((((col >> 3) ^ (row >> 2)) & 1) << 4) + ((col & 7) << 1);
+    else if constexpr (SWZ == 64)
         return row * 64 + ((((col >> 3) ^ (row >> 1)) & 3) << 4) + ((col & 7) << 1);
     else
         return sw128_off(row, col, sub_bytes);
 }
 
-// MN-major operand descriptor of a u_c / v_new / S tile (see tile_off).
-template <bool SW64>
+// MN-major operand descriptor of a u_c / v_new / S tile (see tile_off): MN atoms of
+// SWZ / 2 columns one sub-tile apart, 8-row groups 8 SWZ bytes apart.
+template <int SWZ>
 __device__ __forceinline__ uint64_t umma_desc_mn(uint32_t saddr, uint32_t sub_bytes)
 {
-    if constexpr (SW64)
+    if constexpr (SWZ == 32)
+        return umma_desc_sw32(saddr, sub_bytes, 256);
+    else if constexpr (SWZ == 64)
         return umma_desc_sw64(saddr, sub_bytes, 512);
     else
         return umma_desc_sw128(saddr, sub_bytes, 1024);
@@ -208,29 +227,34 @@ struct StateRegs {
     }
 };
 
-template <int K_, int VT, int STAGES, int EW, bool REF>
-__global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConfig<K_, VT, STAGES, EW>::kMinBlocks)
+template <int K_, int VT, int STAGES, int EW, bool REF, int CH = 1>
+__global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW, CH>::kThreads,
+                                  TcConfig<K_, VT, STAGES, EW, CH>::kMinBlocks)
     fwd_h_tc_kernel(const __grid_constant__ TcArgs args)
 {
-    using Cfg = TcConfig<K_, VT, STAGES, EW>;
+    using Cfg = TcConfig<K_, VT, STAGES, EW, CH>;
     const FwdHParams& p = args.p;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBar);
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    // this warp's chain: an MMA issuer's own, an epilogue warp's column slice (two chains)
+    const int chain = warp > Cfg::kProducerWarp ? warp - Cfg::kMmaWarp
+                                                : (Cfg::kChains == 2 && warp < Cfg::kEpiWarps ? (warp >> 2) : 0);
+
     uint64_t* full = bars;
     uint64_t* empty = bars + STAGES;
-    uint64_t* mma1_done = bars + 2 * STAGES;
+    uint64_t* chain_bars = bars + 2 * STAGES;  // [kChains][5]
+    uint64_t* mma1_done = chain_bars + 5 * chain;
     uint64_t* mma2_done = mma1_done + 1;
     uint64_t* mma_drain = mma1_done + 2;
-    uint64_t* s_ready = mma1_done + 3;     // every epilogue warp wrote its part of S
-    uint64_t* vdec_ready = mma1_done + 4;  // every epilogue warp wrote its rows of v_decay
-    uint64_t* h_read = mma1_done + 5;      // per quadrant (kSharedH): the h store read the state tile
+    uint64_t* s_ready = mma1_done + 3;     // every epilogue warp of the chain wrote its part of S
+    uint64_t* vdec_ready = mma1_done + 4;  // every epilogue warp of the chain wrote its rows of v_decay
+    uint64_t* h_read = chain_bars + 5 * Cfg::kChains;  // per quadrant (kSharedH): the h store read the state tile
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Cfg::kNumBars);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     volatile int* never_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);  // drains ignore aborts
-
-    const int warp = threadIdx.x >> 5;
-    const int lane = threadIdx.x & 31;
 
     if (p.status && (*reinterpret_cast<volatile int*>(p.status) & 0x2)) return;  // bad varlen metadata
 
@@ -251,14 +275,16 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(&full[s], 1 + 32);  // TMA bytes + 32 cp.async arrivals (gate inputs)
-            mbar_init(&empty[s], 1);
+            mbar_init(&empty[s], Cfg::kChains);  // each chain's MMA2 has read the stage
         }
-        mbar_init(mma1_done, 1);
-        mbar_init(mma2_done, 1);
-        mbar_init(s_ready, Cfg::kEpiWarps);
-        mbar_init(vdec_ready, Cfg::kEpiWarps);
+        for (int c = 0; c < Cfg::kChains; ++c) {
+            mbar_init(chain_bars + 5 * c + 0, 1);                              // mma1_done
+            mbar_init(chain_bars + 5 * c + 1, 1);                              // mma2_done
+            mbar_init(chain_bars + 5 * c + 2, 1);                              // drain
+            mbar_init(chain_bars + 5 * c + 3, Cfg::kEpiWarps / Cfg::kChains);  // s_ready
+            mbar_init(chain_bars + 5 * c + 4, Cfg::kEpiWarps / Cfg::kChains);  // vdec_ready
+        }
         for (int q4 = 0; q4 < 4; ++q4) mbar_init(&h_read[q4], EW / 2 > 0 ? EW / 2 : 1);
-        mbar_init(mma_drain, 1);
         *abort_flag = 0;
         *never_flag = 0;
         fence_mbarrier_init();
@@ -330,22 +356,24 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
             for (int64_t c = first; c < issued; ++c)
                 mbar_wait(&full[c % STAGES], static_cast<uint32_t>(c / STAGES) & 1, drain, 0x10);
         }
-    } else if (warp == Cfg::kMmaWarp) {
-        // ------------------------------------------------------------ MMA issuer
+    } else if (warp >= Cfg::kMmaWarp) {
+        // ------------------------------------------------------------ MMA issuer (one per chain)
         // The whole warp runs the loop (descriptors stay warp-uniform); one elected
         // lane issues each MMA and commit, so issue does not stall on a divergent branch.
         auto wait_warp = [&](uint64_t* bar, uint32_t parity) {
             return __all_sync(0xffffffffu, mbar_wait(bar, parity, ctl, 0x20) ? 1 : 0) != 0;
         };
-        const uint32_t d1 = tmem;
-        const uint32_t d2 = tmem + VT;
-        const uint32_t s_addr = sbase + Cfg::kOffS;
+        // the chain's columns: D1 at [c N, c N + N), D2 at VT + that, its sub-tiles of S and u_c
+        const int csub = chain * (Cfg::kChainCols / Cfg::kSubCols);
+        const uint32_t d1 = tmem + static_cast<uint32_t>(chain * Cfg::kChainCols);
+        const uint32_t d2 = tmem + VT + static_cast<uint32_t>(chain * Cfg::kChainCols);
+        const uint32_t s_addr = sbase + Cfg::kOffS + csub * Cfg::kSSubBytes;
         for (int64_t c = 0; c < nchunks; ++c) {
             const int s = static_cast<int>(c % STAGES);
             if (!wait_warp(&full[s], static_cast<uint32_t>(c / STAGES) & 1)) break;
             // descriptors differ only in the start-address field (bits 0-13, 16-byte units)
             const uint64_t a1 = umma_desc_sw128(wc_addr(s), 16, 1024);
-            const uint64_t b1 = umma_desc_mn<Cfg::kSw64>(s_addr, Cfg::kSSubBytes);
+            const uint64_t b1 = umma_desc_mn<Cfg::kSwz>(s_addr, Cfg::kSSubBytes);
             if (!wait_warp(s_ready, static_cast<uint32_t>(c) & 1)) break;
             tc_fence_after();
             if (elect_one_sync()) {
@@ -359,7 +387,7 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
             if (!wait_warp(vdec_ready, static_cast<uint32_t>(c) & 1)) break;
             tc_fence_after();
             const uint64_t a2 = umma_desc_sw128(kc_addr(s), 8192, 1024);
-            const uint64_t b2 = umma_desc_mn<Cfg::kSw64>(uc_addr(s), Cfg::kUSub);
+            const uint64_t b2 = umma_desc_mn<Cfg::kSwz>(uc_addr(s) + csub * Cfg::kUSub, Cfg::kUSub);
             if (elect_one_sync()) {
                 // M = K halves (K = 256): rows 128 m.. of k_c start 2 m sub-tiles in
 #pragma unroll
@@ -498,7 +526,7 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
                     v.y = st.pair_bits(8 * j + 2);
                     v.z = st.pair_bits(8 * j + 4);
                     v.w = st.pair_bits(8 * j + 6);
-                    *reinterpret_cast<uint4*>(s_tile + tile_off<Cfg::kSw64>(row, e2_c0 + 8 * j, Cfg::kSSubBytes)) = v;
+                    *reinterpret_cast<uint4*>(s_tile + tile_off<Cfg::kSwz>(row, e2_c0 + 8 * j, Cfg::kSSubBytes)) = v;
                 }
             } else {
 #pragma unroll
@@ -529,7 +557,7 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
             }
         };
 
-        constexpr int kPairs = (Cfg::kCW / 32) * 8;  // (column block, 8-column group, row half)
+        constexpr int kPairs = Cfg::kCW / 4;  // (column block, 8-column group, row half)
         // Pack v_new after MMA2 is released (64-column tiles); the 10-warp 128-column
         // configuration packs it with v_decay to stay within its register budget.
         constexpr bool kDeferVnew = VT <= 64;
@@ -598,17 +626,23 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
 #pragma unroll
             for (int i = 0; i < kPairs; ++i) {
                 const int cb = i >> 3, j = (i >> 1) & 3, half = i & 1;
-                offs[i] = tile_off<Cfg::kSw64>(half ? tb : ta, cbase + 32 * cb + 8 * j + pc, Cfg::kUSub);
+                offs[i] = tile_off<Cfg::kSwz>(half ? tb : ta, cbase + 32 * cb + 8 * j + pc, Cfg::kUSub);
             }
             uint32_t uraw[kPairs], vds[kPairs], vns[kPairs], vos[kPairs];
 #pragma unroll
             for (int i = 0; i < kPairs; ++i) uraw[i] = *reinterpret_cast<const uint32_t*>(ut + offs[i]);
             if (!mbar_wait(mma1_done, static_cast<uint32_t>(c) & 1, ctl, 0x40)) { ok = false; break; }
             tc_fence_after();
-            uint32_t acc[Cfg::kCW / 32][16];
+            // D1 in 32-column blocks (16 registers each), or one 16-column block
+            constexpr int kAccBlk = Cfg::kCW >= 32 ? Cfg::kCW / 32 : 1;
+            uint32_t acc[kAccBlk][Cfg::kCW >= 32 ? 16 : 8];
 #pragma unroll
-            for (int cb = 0; cb < Cfg::kCW / 32; ++cb)
-                tmem_ld_16x256b_x4(tmem + ((32u * q) << 16) + static_cast<uint32_t>(cbase + 32 * cb), acc[cb]);
+            for (int cb = 0; cb < kAccBlk; ++cb) {
+                if constexpr (Cfg::kCW >= 32)
+                    tmem_ld_16x256b_x4(tmem + ((32u * q) << 16) + static_cast<uint32_t>(cbase + 32 * cb), acc[cb]);
+                else
+                    tmem_ld_16x256b_x2(tmem + ((32u * q) << 16) + static_cast<uint32_t>(cbase), acc[cb]);
+            }
             tmem_wait_ld();
             // v_decay only (the MMA2 operand); v_new is packed after MMA2 is released.
             // Reference arithmetic: when every |u| and every |GEMM output| of the warp lies
@@ -724,7 +758,7 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
 #pragma unroll
                     for (int i = 0; i < kPairs; ++i) {
                         const int j = (i >> 1) & 3, half = i & 1;
-                        *reinterpret_cast<uint32_t*>(vout + vo_base + tile_off<true>(half ? tb : ta, 8 * j + pc, 0)) =
+                        *reinterpret_cast<uint32_t*>(vout + vo_base + tile_off<64>(half ? tb : ta, 8 * j + pc, 0)) =
                             vos[i];
                     }
                 } else {
@@ -777,12 +811,15 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
             };
             bool s_free = true;
             if constexpr (K_ >= 128) {
+                // 32-column blocks of two 16-column loads, or one 16-column load
+                constexpr int kE2Blk = Cfg::kE2Cols >= 32 ? Cfg::kE2Cols / 32 : 1;
+                constexpr int kE2Half = Cfg::kE2Cols >= 32 ? 2 : 1;
                 const uint32_t ta2 = tmem + VT * (1 + (K_ == 256 ? e : 0)) + ((32u * q) << 16) + static_cast<uint32_t>(e2_c0);
 #pragma unroll
-                for (int cb = 0; cb < Cfg::kE2Cols / 32; ++cb) {
-                    uint32_t r[2][16];
-                    tmem_ld_32x32b_x16(ta2 + 32 * cb, r[0]);
-                    tmem_ld_32x32b_x16(ta2 + 32 * cb + 16, r[1]);
+                for (int cb = 0; cb < kE2Blk; ++cb) {
+                    uint32_t r[kE2Half][16];
+#pragma unroll
+                    for (int j = 0; j < kE2Half; ++j) tmem_ld_32x32b_x16(ta2 + 32 * cb + 16 * j, r[j]);
                     if (cb == 0) s_free = wait_s_free();
                     tmem_wait_ld();
                     // Reference arithmetic: the packed chain without saturation applies to a
@@ -792,7 +829,7 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
                     if constexpr (REF) {
                         float m = 0.0f;
 #pragma unroll
-                        for (int j = 0; j < 2; ++j)
+                        for (int j = 0; j < kE2Half; ++j)
 #pragma unroll
                             for (int i = 0; i < 16; ++i) m = fmax_nan(m, fabsf(__uint_as_float(r[j][i])));
                         packed_ref = __all_sync(0xffffffffu, state_ok && alpha <= 1.0f && m < 32768.0f) != 0;
@@ -800,7 +837,7 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
                     if (packed_ref) {
                         const __half2 ah = __float2half2_rn(alpha);
 #pragma unroll
-                        for (int j = 0; j < 2; ++j)
+                        for (int j = 0; j < kE2Half; ++j)
 #pragma unroll
                             for (int i = 0; i < 16; i += 2) {
                                 const int si2 = 32 * cb + 16 * j + i;
@@ -817,7 +854,7 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW>::kThreads, TcConf
                     } else {
                         if constexpr (REF) state_recheck = true;
 #pragma unroll
-                        for (int j = 0; j < 2; ++j)
+                        for (int j = 0; j < kE2Half; ++j)
 #pragma unroll
                             for (int i = 0; i < 16; i += 2) {
                                 const int si2 = 32 * cb + 16 * j + i;

@@ -229,6 +229,14 @@ __device__ __forceinline__ void tmem_ld_16x256b_x4(uint32_t taddr, uint32_t (&r)
         : "r"(taddr));
 }
 
+// The same repeated twice (16 columns): r[4j..4j+3] for j = 0, 1 as above.
+__device__ __forceinline__ void tmem_ld_16x256b_x2(uint32_t taddr, uint32_t (&r)[8])
+{
+    asm volatile("tcgen05.ld.sync.aligned.16x256b.x2.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
+}
+
 // Stores with the 16x256b.x4 fragment layout of tmem_ld_16x256b_x4.
 __device__ __forceinline__ void tmem_st_16x256b_x4(uint32_t taddr, const uint32_t (&r)[16])
 {
@@ -269,6 +277,19 @@ __device__ __forceinline__ uint64_t umma_desc_sw64(uint32_t saddr, uint32_t lbo,
     d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
     d |= 1ull << 46;  // descriptor version for tcgen05
     d |= 4ull << 61;  // SWIZZLE_64B
+    return d;
+}
+
+// The same with the 32-byte swizzle (layout type 6): 32-byte rows, 8-row groups
+// `sbo` apart; for MN-major operands one atom is 16 elements wide.
+__device__ __forceinline__ uint64_t umma_desc_sw32(uint32_t saddr, uint32_t lbo, uint32_t sbo)
+{
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+    d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+    d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+    d |= 1ull << 46;  // descriptor version for tcgen05
+    d |= 6ull << 61;  // SWIZZLE_32B
     return d;
 }
 

@@ -124,7 +124,10 @@ typedef struct {
     int32_t fault_inject;            /* test hook: 1 makes the load producer
                                         stop after chunk 0 so that the bounded
                                         waits expire; 0 in production */
-    int32_t reserved;
+    int32_t chains;                  /* 0 auto, 1, or 2: the two column halves
+                                        of a V tile run as independent chains
+                                        in one CTA (64 < K <= 128 with v_tile
+                                        32 or 128) */
 } cgdrFwdHOptions;
 
 /* Launch plan chosen in phase 1 (the counterpart of the reference's tiling
@@ -140,6 +143,9 @@ typedef struct {
     int32_t grid, block, smem_bytes, stages;
     int32_t numerics, layout;
     uint64_t workspace_bytes;
+    int32_t chains;          /* chains per CTA (each v_tile / chains columns);
+                                task_count counts chains, grid CTAs */
+    int32_t reserved;
 } cgdrFwdHPlan;
 
 typedef struct cgdrExecutor cgdrExecutor;

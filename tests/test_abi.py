@@ -191,7 +191,9 @@ def test_plan_varlen_all_optional_paths():
     assert (pl["total_tokens"], pl["sequence_count"], pl["chunk_count"]) == (10016, 2, 158)
     assert (pl["value_heads"], pl["key_heads"], pl["head_ratio"]) == (8, 2, 4)
     assert pl["kernel"] == 1 and pl["v_tile"] in (32, 64, 128)
-    assert pl["task_count"] == 2 * 8 * pl["v_tile_count"] == pl["grid"]
+    # the reference arithmetic runs two chains per CTA where the tile is built for them
+    assert pl["task_count"] == 2 * 8 * pl["v_tile_count"] * pl["chains"]
+    assert pl["grid"] == 2 * 8 * pl["v_tile_count"]
     assert pl["workspace_bytes"] >= 256 + 4 * 3 + 4 * 2
 
 
@@ -201,7 +203,8 @@ def test_plan_fixed_length_without_optional_state_or_final():
     d["final_state"] = None
     pl = phase1(d).plan
     assert pl["plan_key"] == 0
-    assert (pl["sequence_count"], pl["chunk_count"], pl["task_count"]) == (1, 2, 4 * pl["v_tile_count"])
+    assert (pl["sequence_count"], pl["chunk_count"]) == (1, 2)
+    assert pl["task_count"] == 4 * pl["v_tile_count"] * pl["chains"]
     assert pl["workspace_bytes"] == 256
 
 
@@ -302,21 +305,44 @@ def test_python_front_end_refuses_cpu_tensors():
     (4, 32, 128, 96, 32),    # V % 64 != 0 (K = 128): 32-column tiles whatever the task count
 ])
 def test_plan_v_tile_choice(B, H, K, V, expected):
-    """The planner takes the narrowest V tile that keeps one CTA per SM (148 SMs)."""
+    """The planner takes the narrowest V tile that keeps one CTA per SM (148 SMs),
+    one chain per CTA for the fp32-state arithmetic and two for the reference
+    arithmetic where the tile is built for them (32 and 128 columns, K tile 128)."""
     T = 256
     op = cg.ChunkGatedDeltaRuleFwdH(e((B, T, H, K)), e((B, T, H, K)), e((B, T, H, V)), e((B, T, H), F32), None,
                                     None, None, 64, e((B, T // 64, H, K, V)), e((B, T, H, V)), e((B, H, K, V), F32),
                                     layout="token_major", numerics="fp32_state")
-    assert op.plan["v_tile"] == expected
+    assert (op.plan["v_tile"], op.plan["chains"]) == (expected, 1)
+    op = cg.ChunkGatedDeltaRuleFwdH(e((B, T, H, K)), e((B, T, H, K)), e((B, T, H, V)), e((B, T, H), F32), None,
+                                    None, None, 64, e((B, T // 64, H, K, V)), e((B, T, H, V)), e((B, H, K, V), BF),
+                                    layout="token_major", numerics="reference")
+    assert (op.plan["v_tile"], op.plan["chains"]) == (expected, 2 if K == 128 and expected in (32, 128) else 1)
 
 
-def test_plan_rejects_v_tile_32_with_k_64():
+@pytest.mark.parametrize("K,vt,chains", [(64, 32, 0), (64, 32, 2), (64, 128, 2), (128, 64, 2), (256, 64, 2),
+                                         (128, 128, 3)])
+def test_plan_rejects_unbuilt_tile_and_chain_choices(K, vt, chains):
     B, T, H = 1, 128, 2
     with pytest.raises(cg.CgdrError) as ei:
-        cg.ChunkGatedDeltaRuleFwdH(e((B, T, H, 64)), e((B, T, H, 64)), e((B, T, H, 64)), e((B, T, H), F32), None,
-                                   None, None, 64, e((B, 2, H, 64, 64)), e((B, T, H, 64)), None,
-                                   layout="token_major", numerics="fp32_state", v_tile=32)
+        cg.ChunkGatedDeltaRuleFwdH(e((B, T, H, K)), e((B, T, H, K)), e((B, T, H, K)), e((B, T, H), F32), None,
+                                   None, None, 64, e((B, 2, H, K, K)), e((B, T, H, K)), None,
+                                   layout="token_major", numerics="fp32_state", v_tile=vt, chains=chains)
     assert ei.value.status_name == "UNSUPPORTED"
+
+
+@pytest.mark.parametrize("vt,V", [(32, 128), (32, 48), (128, 256), (128, 192)])
+def test_plan_two_chains_per_cta(vt, V):
+    """chains 2: each V tile's two column halves are chains of their own in one CTA
+    (eight epilogue warps, a producer and one MMA issuer per chain); task_count
+    counts chains, grid CTAs."""
+    B, T, H, K = 2, 256, 4, 128
+    op = cg.ChunkGatedDeltaRuleFwdH(e((B, T, H, K)), e((B, T, H, K)), e((B, T, H, V)), e((B, T, H), F32), None,
+                                    None, None, 64, e((B, T // 64, H, K, V)), e((B, T, H, V)), e((B, H, K, V), F32),
+                                    layout="token_major", numerics="fp32_state", v_tile=vt, chains=2)
+    pl = op.plan
+    assert (pl["kernel"], pl["v_tile"], pl["chains"], pl["block"]) == (1, vt, 2, 32 * 11)
+    assert pl["v_tile_count"] == (V + vt - 1) // vt and pl["grid"] == B * H * pl["v_tile_count"]
+    assert pl["task_count"] == 2 * pl["grid"]
 
 
 # ---- host-memory front end: the pipeline's pieces (pure host logic) -------------

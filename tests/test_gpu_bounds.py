@@ -88,9 +88,10 @@ def _shapes(t):
     return ci, (B, NT, H_, K, V), (B, T, H_, V), (N, H_, K, V)
 
 
-def _launch(t, ci, h, v, f, numerics, kernel, no_alloc=False):
+def _launch(t, ci, h, v, f, numerics, kernel, no_alloc=False, v_tile=0, chains=0):
     op = cg.ChunkGatedDeltaRuleFwdH(t["k"], t["w"], t["u"], t["g"], t["initial_state"], t["cu_seqlens"], ci, 64,
-                                    h, v, f, layout="token_major", numerics=numerics, force_kernel=kernel)
+                                    h, v, f, layout="token_major", numerics=numerics, force_kernel=kernel,
+                                    v_tile=v_tile, chains=chains)
     if no_alloc:
         ex, op._ex = op._ex, None
         status = ctypes.c_int32(-1)
@@ -104,10 +105,17 @@ def _launch(t, ci, h, v, f, numerics, kernel, no_alloc=False):
         assert cg.read_device_status(ws) == 0
 
 
-@pytest.mark.parametrize("K,V", [(128, 128), (64, 64), (32, 32), (96, 96), (256, 256), (64, 96)])
+@pytest.mark.parametrize("K,V,v_tile,chains", [(128, 128, 0, 0), (64, 64, 0, 0), (32, 32, 0, 0), (96, 96, 0, 0),
+                                                (256, 256, 0, 0), (64, 96, 0, 0), (128, 128, 32, 2), (96, 48, 32, 2),
+                                                (128, 192, 128, 2)])
 @pytest.mark.parametrize("kernel", [1, 2])
 @pytest.mark.parametrize("numerics", ["fp32_state", "reference"])
-def test_outputs_stay_inside_their_extent(K, V, kernel, numerics):
+def test_outputs_stay_inside_their_extent(K, V, v_tile, chains, kernel, numerics):
+    """Two chains per CTA run on the tensor-core kernel only; with V = 48 (32-column
+    tiles) and V = 192 (128-column tiles) the last CTA's second chain lies wholly
+    past V."""
+    if chains and kernel != 1:
+        pytest.skip("the V tile and chain options apply to the tensor-core kernel")
     dev = _cuda()
     t = _inputs(K, V, dev, seed=K + 3 * V)
     ci, hs, vs, fs = _shapes(t)
@@ -115,7 +123,7 @@ def test_outputs_stay_inside_their_extent(K, V, kernel, numerics):
     if numerics == "reference":
         t["initial_state"] = t["initial_state"].to(torch.bfloat16)
     gh, gv, gf = Guarded(hs, torch.bfloat16, dev), Guarded(vs, torch.bfloat16, dev), Guarded(fs, fdt, dev)
-    _launch(t, ci, gh.view, gv.view, gf.view, numerics, kernel)
+    _launch(t, ci, gh.view, gv.view, gf.view, numerics, kernel, v_tile=v_tile, chains=chains)
     torch.cuda.synchronize()
     for name, gd in (("h", gh), ("v_new", gv), ("final_state", gf)):
         n_bad, first = gd.guards_intact()
@@ -124,7 +132,7 @@ def test_outputs_stay_inside_their_extent(K, V, kernel, numerics):
     h = torch.empty(hs, dtype=torch.bfloat16, device=dev)
     v = torch.empty(vs, dtype=torch.bfloat16, device=dev)
     f = torch.empty(fs, dtype=fdt, device=dev)
-    _launch(t, ci, h, v, f, numerics, kernel)
+    _launch(t, ci, h, v, f, numerics, kernel, v_tile=v_tile, chains=chains)
     torch.cuda.synchronize()
     for name, a, b in (("h", gh.view, h), ("v_new", gv.view, v), ("final_state", gf.view, f)):
         assert torch.equal(a, b), f"{name}: strided outputs differ from contiguous ones"

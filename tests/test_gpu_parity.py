@@ -417,19 +417,22 @@ def test_device_chunk_list_pads_everything_for_bad_lengths():
 @pytest.mark.parametrize("varlen", [False, True])
 @pytest.mark.parametrize("V,HK", [(128, 4), (256, 2)])
 def test_v_tiles_agree(numerics, varlen, V, HK):
-    """32-, 64- and 128-column V tiles compute every column with the same products
-    and roundings (columns are independent in both contractions and in the state
-    update), so their outputs are bit-identical; 32-column tiles keep u, v_new and
-    the state in 64-byte-swizzled tiles, the others in 128-byte ones."""
+    """32-, 64- and 128-column V tiles, each one chain or (32 and 128) two chains of
+    half the width, compute every column with the same products and roundings
+    (columns are independent in both contractions and in the state update), so their
+    outputs are bit-identical; 32-column tiles keep u, v_new and the state in
+    64-byte-swizzled tiles, their two 16-column chains in 32-byte-swizzled ones, the
+    others in 128-byte ones."""
     dev = _cuda()
     if varlen:
         inp = H.make_inputs(1, 700, 4, 128, V, HK=HK, seed=21, cu_seqlens=[0, 300, 337, 401, 700])
     else:
         inp = H.make_inputs(2, 333, 4, 128, V, HK=HK, seed=21)
-    outs = [_run_fla(inp, dev, numerics=numerics, force_kernel=1, v_tile=vt) for vt in (32, 64, 128)]
-    for vt, o in zip((64, 128), outs[1:]):
+    tiles = ((32, 1), (32, 2), (64, 1), (128, 1), (128, 2))
+    outs = [_run_fla(inp, dev, numerics=numerics, force_kernel=1, v_tile=vt, chains=ch) for vt, ch in tiles]
+    for (vt, ch), o in zip(tiles[1:], outs[1:]):
         for name, a, b in zip(("h", "v", "final"), outs[0], o):
-            assert torch.equal(a, b), f"v_tile 32 vs {vt}: {name} differs"
+            assert torch.equal(a, b), f"v_tile 32 vs {vt} with {ch} chain(s): {name} differs"
 
 
 @pytest.mark.parametrize("V", [32, 96])
