@@ -449,11 +449,12 @@ __global__ void __launch_bounds__(TcConfig<K_, VT, STAGES, EW, CH>::kThreads,
         // K=128: this thread's kCW state values are one contiguous run of a row
         // when V is the unit-stride dimension; 16-byte loads then take a quarter
         // (fp32) or an eighth (bf16) of the L1 wavefronts of scalar loads, whose
-        // 32 lanes each touch a different row.  Built for the 128-column fp32-state
-        // kernel only: in the 64-column and reference-arithmetic kernels the extra
+        // 32 lanes each touch a different row.  Built for the fp32-state 128-column
+        // and single-chain 32-column kernels (B=2 T=4096 H=16: 0.093-0.095 ->
+        // 0.090-0.092 ms): in the 64-column and reference-arithmetic kernels the extra
         // code slowed the chunk loop more than it saved (1.42 -> 1.52 ms on a
         // 1024-chunk chain; 0.52 -> 0.55 ms with the rounding chain).
-        constexpr bool kVecState = ((K_ == 128 && VT == 128) || K_ == 256) && !REF;
+        constexpr bool kVecState = ((K_ == 128 && (VT == 128 || (VT == 32 && CH == 1))) || K_ == 256) && !REF;
         const size_t h0_esz = p.h0_dtype == kBF16 ? 2 : 4;
         const uint8_t* h0_run = nullptr;
         // a whole run inside the caller's K x V state
