@@ -476,3 +476,51 @@ def test_head_widths_on_tensor_cores(K, V, varlen):
         gh, gv, gf = _run_fla(inp, dev, numerics=numerics, force_kernel=2)
         H.assert_close(h, gh, BF_TOL, BF_TOL, f"K{K} V{V} {numerics}/h tc vs general")
         H.assert_close(f, gf, BF_TOL, BF_TOL, f"K{K} V{V} {numerics}/final tc vs general")
+
+
+@pytest.mark.parametrize("numerics", ["fp32_state", "reference"])
+def test_multi_wave_batch_matches_single_wave_groups(numerics):
+    """More tasks than resident CTAs: 200 packed sequences x 4 heads are 800 CTAs of
+    128 columns, several waves on 148 SMs, in the longest-first order.  The same sequences
+    run in groups of 30 (120 CTAs, one wave) give bit-identical outputs.  The batch holds
+    empty sequences, one-token ones and partial chunks."""
+    dev = _cuda()
+    rng = np.random.default_rng(5)
+    lens = [int(x) for x in rng.integers(0, 300, size=200)]
+    lens[3] = lens[50] = 0
+    lens[199] = 1
+    cu = [0]
+    for L in lens:
+        cu.append(cu[-1] + L)
+    heads = 4
+    inp = H.make_inputs(1, cu[-1], heads, 128, 128, seed=31, cu_seqlens=cu)
+    if numerics == "reference":
+        inp["initial_state"] = inp["initial_state"].to(torch.bfloat16)
+    fdt = torch.float32 if numerics == "fp32_state" else torch.bfloat16
+    h, v, f = _run_fla(inp, dev, numerics=numerics, final_state_dtype=fdt)
+    chunk0 = [0]
+    for L in lens:
+        chunk0.append(chunk0[-1] + (L + 63) // 64)
+    for a in range(0, len(lens), 30):
+        b = min(a + 30, len(lens))
+        t0, t1 = cu[a], cu[b]
+        part = {n: inp[n][:, t0:t1] for n in ("k", "w", "u", "g")}
+        part["initial_state"] = inp["initial_state"][a:b]
+        part["cu_seqlens"] = torch.tensor([x - t0 for x in cu[a:b + 1]], dtype=torch.int64)
+        hp, vp, fp = _run_fla(part, dev, numerics=numerics, final_state_dtype=fdt)
+        assert torch.equal(hp, h[:, chunk0[a]:chunk0[b]]), f"h of sequences {a}..{b - 1}"
+        assert torch.equal(vp, v[:, t0:t1]), f"v_new of sequences {a}..{b - 1}"
+        assert torch.equal(fp, f[a:b]), f"final state of sequences {a}..{b - 1}"
+
+
+def test_multi_wave_fixed_length_matches_rows():
+    """Fixed length with more (sequence, head) tasks than resident CTAs (8 x 40 = 320
+    CTAs, three waves): bit-identical to the rows run one at a time (one wave each)."""
+    dev = _cuda()
+    inp = H.make_inputs(8, 333, 40, 128, 128, seed=32)
+    h, v, f = _run_fla(inp, dev, numerics="fp32_state")
+    for b in range(8):
+        row = {n: inp[n][b:b + 1] for n in ("k", "w", "u", "g")}
+        row["initial_state"] = inp["initial_state"][b:b + 1]
+        hr, vr, fr = _run_fla(row, dev, numerics="fp32_state")
+        assert torch.equal(hr, h[b:b + 1]) and torch.equal(vr, v[b:b + 1]) and torch.equal(fr, f[b:b + 1]), b
